@@ -1,0 +1,349 @@
+"""Benchmark of the quantised linear (libsdq) on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
+    python bench.py --impl reference ...      # the CPU arm (oracle port of the reference)
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workloads (data synthetic, seeded):
+  cfg2  (default) X bf16 [4096, 12288] . W [3072, 12288]^T, W8 g64  -- configs[1]
+  cfg1  X [1024, 3072] . W [3072, 3072]^T, W4
+  cfg3  X [M<=8, 3072] . W [18432, 3072]^T, W4 (HBM-bound; reports GB/s)
+  cfg5  X [16384, 3072] . W [12288, 3072]^T, W4
+A step is one quantised matmul over the workload's X with the weight resident in HBM.
+With N > 1 ranks each rank holds one workload-sized column shard of a weight N times
+as wide (weak scaling) and the [M, N*n] output is all-gathered over NVLink (NCCL).
+
+Timing: W untimed warm-up steps, then K timed steps bracketed by barrier + synchronize;
+L2 is flushed (a 256 MiB write) before every step outside the timed events, and each
+step is timed with CUDA events on the launching stream; the total is max-reduced over
+ranks.  `e2e` repeats the step through the public API with the step's X copied from
+pinned host memory and the (gathered) Y copied back inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "stable-diffusion.rs_b200"))
+
+WORKLOADS = {
+    # name: (M, K, N, bits, sigma_w, metric kind)
+    "cfg1": (1024, 3072, 3072, 4, 0.02, "tflops"),
+    "cfg2": (4096, 12288, 3072, 8, 0.01, "tflops"),
+    "cfg3": (8, 3072, 18432, 4, 0.02, "gbs"),
+    "cfg5": (16384, 3072, 12288, 4, 0.02, "tflops"),
+}
+DESCR = {
+    "cfg1": "BASELINE configs[0]: X bf16[1024,3072] . W[3072,3072]^T, W4 g64",
+    "cfg2": "BASELINE configs[1]: X bf16[4096,12288] . W[3072,12288]^T, W8 g64 (Flux MLP down-proj at 1024^2)",
+    "cfg3": "BASELINE configs[2]: X bf16[8,3072] . W[18432,3072]^T, W4 g64 (adaLN modulation, small-M)",
+    "cfg5": "BASELINE configs[4]: X bf16[16384,3072] . W[12288,3072]^T, W4 g64",
+}
+
+
+def algorithmic(m, k, n, bits, world=1):
+    """(flops, bytes) of one step on one rank: 2*M*N*K, and packed W + S + B + X + Y (each once)."""
+    flops = 2.0 * m * n * k
+    byts = n * k * bits / 8 + 2 * n * (k // 64) * 2 + m * k * 2 + m * n * 2
+    return flops, byts
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def traffic_from_profiles(workload):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"traffic_{workload}.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.out = out
+        else:
+            self.out = ""
+
+    def summary(self):
+        rows = [r.split(", ") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        load = [v for v in sm if v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_reference(args, wl):
+    """The reference's algorithm on the host cores: the oracle port (the reference's MLX CPU
+    backend is not installable here), on a bounded sample of the workload's rows."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    m, k, n, bits, sig, kind = WORKLOADS[wl]
+    threads = O.max_threads()
+    ms = min(m, 8 if kind == "gbs" else 48)     # sample rows of X per step
+    ns = n if kind == "gbs" else min(n, 3072)
+    xb, w = O.synthetic_linear(1234, ms, k, ns, sig)
+    wq, s, b = O.quantize(w, bits)
+    for _ in range(max(1, args.warmup // 3)):
+        O.qmatmul(xb, wq, s, b, ns, bits, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.qmatmul(xb, wq, s, b, ns, bits, threads=threads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    flops, byts = algorithmic(ms, k, ns, bits)
+    value = (flops / t / 1e12) if kind == "tflops" else (byts / t / 1e9)
+    sample = f"X rows {ms} of {m}, W rows {ns} of {n}, K={k}, W{bits}; median of {len(times)}"
+    return value, threads, sample
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="sdq", choices=["sdq", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = args.workload
+    m, k, n, bits, sig, kind = WORKLOADS[wl]
+    metric = "qmatmul_tflops" if kind == "tflops" else "qmatmul_hbm_gbs"
+    unit = "TFLOP/s" if kind == "tflops" else "GB/s"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        value, threads, sample = cpu_reference(args, wl)
+        print(json.dumps({
+            "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (SeededRng)",
+            "config": {"workload": wl, "descr": DESCR[wl], "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    import torch
+    import sdq
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+
+    # ---- data: X replicated, this rank's W shard (rows rank*n .. rank*n + n of a [world*n, k] W)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    gx = torch.Generator(device=dev).manual_seed(999)
+    x = torch.randn(m, k, device=dev, generator=gx).to(torch.bfloat16)
+    w = torch.randn(n, k, device=dev, generator=g) * sig
+    wq, s, b = sdq.quantize(w, 64, bits)
+    del w
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    comm = None
+    if world > 1:
+        uid = [sdq.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = sdq.Comm(uid[0], world, rank)
+        y_shards = torch.empty((world, m, n), device=dev, dtype=torch.bfloat16)
+        y_full = torch.empty((m, world * n), device=dev, dtype=torch.bfloat16)
+    y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+
+    def step():
+        if comm is None:
+            sdq.quantized_matmul(x, wq, s, b, 64, bits, out=y)
+        else:
+            sdq.quantized_matmul_sharded(x, wq, s, b, comm, 64, bits, y_shards=y_shards, out=y_full)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    sdq.device_status()
+
+    # ---- device-resident timing (value): K steps, per-step CUDA events, L2 flushed before each
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        barrier()
+    sdq.device_status()
+    step_ms = [a.elapsed_time(bb) for a, bb in ev]
+    total_ms = sum(step_ms)
+    if dist is not None:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+
+    # ---- the dominant kernel alone (for the roofline): at N = 1 it is the whole step
+    if comm is None:
+        kern_ms = step_ms
+    else:
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            kev[i][0].record(stream)
+            sdq.quantized_matmul(x, wq, s, b, 64, bits, out=y)
+            kev[i][1].record(stream)
+        torch.cuda.synchronize()
+        kern_ms = [a.elapsed_time(bb) for a, bb in kev]
+
+    flops, byts = algorithmic(m, k, n, bits)
+    if kind == "tflops":
+        value = flops * world / (ms_per_step * 1e-3) / 1e12
+    else:
+        value = byts * world / (ms_per_step * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers
+    xh = torch.empty((m, k), dtype=torch.bfloat16, pin_memory=True)
+    xh.copy_(x.cpu())
+    yh = torch.empty((m, n * world), dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        if i >= args.warmup:
+            e2e_ev[i - args.warmup][0].record(stream)
+        xd.copy_(xh, non_blocking=True)
+        if comm is None:
+            sdq.quantized_matmul(xd, wq, s, b, 64, bits, out=y)
+            yh.copy_(y, non_blocking=True)
+        else:
+            sdq.quantized_matmul_sharded(xd, wq, s, b, comm, 64, bits, y_shards=y_shards, out=y_full)
+            yh.copy_(y_full, non_blocking=True)
+        if i >= args.warmup:
+            e2e_ev[i - args.warmup][1].record(stream)
+    barrier()
+    e2e_ms = sum(a.elapsed_time(bb) for a, bb in e2e_ev)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_step = e2e_ms / args.steps
+    e2e_value = (flops if kind == "tflops" else byts) * world / (e2e_step * 1e-3) / (1e12 if kind == "tflops" else 1e9)
+
+    # ---- roofline of the dominant kernel (the qmm kernel, CUDA events around its launches)
+    hbm, tc, src = peaks()
+    kern_avg = sum(kern_ms) / len(kern_ms)
+    if kind == "tflops":
+        achieved = flops / (kern_avg * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tc, "unit": "TFLOP/s",
+                "frac": achieved / tc, "peak_source": f"{src} burst bf16 (MEASURED_PEAKS.json)"}
+    else:
+        achieved = byts / (kern_avg * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": f"{src} copy bandwidth (MEASURED_PEAKS.json)"}
+    roof["traffic"] = traffic_from_profiles(wl)
+    roof["kernel_ms"] = kern_avg
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cv, threads, sample = cpu_reference(argparse.Namespace(steps=3, warmup=3), wl)
+        cpu = {"value": cv, "unit": unit, "cores": threads, "kind": "port", "sample": sample}
+
+    if comm is not None:
+        comm.destroy()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded torch normal; weights quantised by libsdq)",
+            "config": {"workload": wl, "descr": DESCR[wl], "M": m, "K": k, "N_per_rank": n, "bits": bits,
+                       "group_size": 64, "global_N": n * world,
+                       "parallelism": "single GPU" if world == 1 else f"N-sharded x{world} + NCCL all-gather",
+                       "l2": "flushed before every step (256 MiB write, outside the timed events)"},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_step,
+                    "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * world * 2,
+                    "path": "sdq.quantized_matmul%s (C ABI) with pinned host X in, Y out" %
+                            ("" if world == 1 else "_sharded")},
+            "gpu_launches": args.steps * (1 if world == 1 else 2),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+/*
+ * sdq.h -- C ABI of libsdq, a B200 (sm_100a) CUDA library for the affine
+ * group-wise quantised linear of andreinknv/stable-diffusion.rs.
+ *
+ * This ABI replaces the three mlx-c entry points that the reference's
+ * `sd-tensor` seam binds for `QuantizedArray` (crates/sd-tensor/src/mlx.rs:
+ * 361-397) -- mlx_quantize, mlx_dequantize and mlx_quantized_matmul -- with
+ * plain pointers and sizes.  Conventions mirror the reference's FFI:
+ *
+ *   - every entry point returns an int status, 0 = success (mlx.rs:448-470);
+ *   - on failure the message is kept per thread and read with
+ *     sdq_last_error() (the thread-local handler of mlx.rs:419-446);
+ *   - no C++ exception crosses the boundary;
+ *   - the library never frees caller memory; all tensors are caller-allocated
+ *     DEVICE buffers (cudaMalloc'd or equivalent);
+ *   - every call takes an explicit CUDA stream (`void*` = cudaStream_t, NULL =
+ *     legacy default stream), mirroring the per-call mlx_stream, and is
+ *     asynchronous on it.  The caller synchronises, as the reference's
+ *     `eval` does (mlx.rs:1531-1544).
+ *
+ * There is no CPU fallback: a call on a machine without an sm_100 device
+ * fails with SDQ_ERR_CUDA.
+ *
+ * Tensor layouts (row-major, contiguous):
+ *   W   [n, k]                   dense weight, `[out, in]` (diffusers Linear)
+ *   Wq  [n, k * bits / 32] u32   element k of a row in word k / (32/bits) at
+ *                                bit offset bits * (k % (32/bits)) (little-end)
+ *   S,B [n, k / group_size]      per-group scale and bias
+ *   X   [m, k]                   activations
+ *   Y   [m, n]                   Y = X . dequant(W)^T (+ bias[n])
+ *
+ * Supported today: group_size 64, bits 4 or 8, mode "affine", transpose true,
+ * k % 64 == 0, X/Y/S/B bf16 (weights to quantise: f32 or bf16).  Anything
+ * else is rejected with SDQ_ERR_UNSUPPORTED or SDQ_ERR_INVALID and a message.
+ */
+#ifndef SDQ_H
+#define SDQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SDQ_ABI_VERSION 1
+
+/* Status codes. */
+#define SDQ_OK 0
+#define SDQ_ERR_INVALID 1     /* bad argument: null pointer, shape, alignment */
+#define SDQ_ERR_UNSUPPORTED 2 /* valid in MLX but not provided here (bits 2/3/5/6, f16 ...) */
+#define SDQ_ERR_CUDA 3        /* a CUDA runtime / driver call failed */
+#define SDQ_ERR_TIMEOUT 4     /* a device-side wait exceeded its limit (kernel returned early) */
+#define SDQ_ERR_NCCL 5        /* an NCCL call failed */
+
+/* Element types (values fixed; they are part of the ABI). */
+typedef enum sdq_dtype {
+    SDQ_F32 = 0,
+    SDQ_BF16 = 1,
+    SDQ_F16 = 2
+} sdq_dtype;
+
+/* The last error message on this thread, or "" when the last call succeeded.
+ * Replaces the error-handler trampoline of mlx.rs:432-446. */
+const char* sdq_last_error(void);
+
+/* ABI version (SDQ_ABI_VERSION) the library was built with. */
+int sdq_abi_version(void);
+
+/*
+ * Quantise a dense weight.
+ * Replaces mlx_quantize (mlx.rs:362-370) as called by QuantizedArray::quantize
+ * (mlx.rs:1861-1911): w [n,k] (w_dtype) -> wq, scales, biases (sb_dtype).
+ * group_size / bits <= 0 select the defaults 64 / 4, as an absent
+ * mlx_optional_int does.  mode NULL means "affine".
+ */
+int sdq_quantize(const void* w, sdq_dtype w_dtype, int64_t n, int64_t k, int group_size,
+                 int bits, const char* mode, uint32_t* wq, void* scales, void* biases,
+                 sdq_dtype sb_dtype, void* stream);
+
+/*
+ * Reconstruct the dense weight: out[n,k] = s * q + b, rounded once to
+ * out_dtype.  Replaces mlx_dequantize (mlx.rs:373-384) as called by
+ * QuantizedArray::dequantize (mlx.rs:1918-1945).  For tests and for layers
+ * without a quantised kernel; not the hot path.
+ */
+int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases,
+                   sdq_dtype sb_dtype, int64_t n, int64_t k, int group_size, int bits,
+                   const char* mode, void* out, sdq_dtype out_dtype, void* stream);
+
+/*
+ * y[m,n] = x[m,k] . dequant(wq, scales, biases)[n,k]^T (+ bias[n] when bias is
+ * non-NULL), dequantising inside the kernel.  Replaces mlx_quantized_matmul
+ * (mlx.rs:386-397) as called by QuantizedArray::matmul (mlx.rs:1952-1975) and,
+ * with `bias`, the separate `y.add(bias)` of quantized::linear
+ * (crates/sd-models/src/mlx/quantized.rs:314-317).  `transpose` must be true
+ * (the reference always passes true).  m >= 1.  m <= 8 with k <= 12288 runs
+ * the HBM-streaming small-M kernel; anything else runs the tcgen05
+ * tensor-core kernel.  x and wq must be 16-byte aligned.
+ */
+int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                         const uint32_t* wq, const void* scales, const void* biases,
+                         sdq_dtype sb_dtype, int64_t n, int transpose, int group_size, int bits,
+                         const char* mode, const void* bias, void* y, sdq_dtype y_dtype,
+                         void* stream);
+
+/*
+ * Bytes a quantised [n,k] weight occupies, packed words plus scales and
+ * biases, with sb_bytes per scale/bias element (the reference counts 4,
+ * mlx.rs:1981-1985; this library stores bf16, 2).  Returns 0 on invalid
+ * arguments.
+ */
+size_t sdq_resident_bytes(int64_t n, int64_t k, int group_size, int bits, int sb_bytes);
+
+/*
+ * Read back and clear the device-side status word that the kernels set when a
+ * bounded wait gives up.  Synchronises `stream`.  Returns SDQ_OK or
+ * SDQ_ERR_TIMEOUT (with a message naming the wait).  No counterpart in the
+ * reference (MLX kernels have no device-side waits).
+ */
+int sdq_device_status(void* stream);
+
+/*
+ * Communicators for the column-sharded linear.  The library owns its NCCL
+ * communicator, so no NCCL type crosses the ABI: rank 0 calls
+ * sdq_comm_unique_id, shares the 128 bytes with the other ranks by any means
+ * (a store, a file, MPI), then every rank calls sdq_comm_init on its own
+ * device.  No counterpart in the reference (single-device; crates/sd-tensor
+ * has no collectives).
+ */
+int sdq_comm_unique_id(uint8_t out_id[128]);
+int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out);
+int sdq_comm_destroy(void* comm);
+
+/*
+ * Column-sharded quantised linear: this rank holds rows
+ * [rank*n_local, (rank+1)*n_local) of the weight (wq/scales/biases/bias_local
+ * are the local shard).  It computes y_local[m, n_local] into
+ * y_shards + rank*m*n_local, all-gathers in place over NVLink so that every
+ * rank's y_shards holds [world, m, n_local], and, when y is non-NULL,
+ * permutes that into y[m, world*n_local].  y_shards is caller-provided
+ * (world*m*n_local elements, 16-byte aligned).  The compute step is
+ * sdq_quantized_matmul; the exchange is one ncclAllGather on `stream`.
+ */
+int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                                 const uint32_t* wq, const void* scales, const void* biases,
+                                 sdq_dtype sb_dtype, int64_t n_local, int group_size, int bits,
+                                 const void* bias_local, void* y_shards, void* y,
+                                 sdq_dtype y_dtype, void* comm, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SDQ_H */

@@ -1,0 +1,233 @@
+// sdq_api.cu -- the C ABI (include/sdq.h): argument validation, per-thread
+// error messages, and kernel selection.  No CPU fallback: without an sm_100
+// device every compute entry point fails with SDQ_ERR_CUDA.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/sdq.h"
+#include "sdq_internal.h"
+
+namespace sdq {
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int ok() {
+    t_last_error.clear();
+    return SDQ_OK;
+}
+
+int cuda_fail(const char* what, cudaError_t e) {
+    return fail(SDQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+struct DevInfo {
+    bool probed = false;
+    bool supported = false;
+    int sms = 0;
+    int major = 0, minor = 0;
+};
+DevInfo g_dev[64];
+
+// Ensure the current device is an sm_100 part (the library carries sm_100a
+// code only).  Returns SDQ_OK or an error code with the message set.
+int check_device() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail("no CUDA device", e);
+    if (dev < 0 || dev >= 64) return fail(SDQ_ERR_CUDA, "device ordinal %d out of range", dev);
+    DevInfo& d = g_dev[dev];
+    if (!d.probed) {
+        if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+            (e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail("cudaDeviceGetAttribute", e);
+        d.supported = d.major == 10 && d.minor == 0;
+        d.probed = true;
+    }
+    if (!d.supported)
+        return fail(SDQ_ERR_CUDA, "device %d is sm_%d%d; libsdq carries sm_100a code only", dev,
+                    d.major, d.minor);
+    return SDQ_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Shared checks of the quantisation parameters; resolves defaults in place.
+int check_qparams(int& group_size, int& bits, const char* mode, const char* fn) {
+    if (group_size <= 0) group_size = 64;
+    if (bits <= 0) bits = 4;
+    if (mode != nullptr && std::strcmp(mode, "affine") != 0)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: mode \"%s\" is not supported (only \"affine\")", fn,
+                    mode);
+    if (group_size != 64)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: group_size %d is not supported (only 64)", fn,
+                    group_size);
+    if (bits == 2 || bits == 3 || bits == 5 || bits == 6)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: bits %d is not supported (only 4 and 8)", fn, bits);
+    if (bits != 4 && bits != 8)
+        return fail(SDQ_ERR_INVALID, "%s: bits must be one of 2, 3, 4, 5, 6, 8; got %d", fn, bits);
+    return SDQ_OK;
+}
+
+int check_nk(int64_t n, int64_t k, const char* fn) {
+    if (n <= 0) return fail(SDQ_ERR_INVALID, "%s: n (rows, out features) must be >= 1; got %lld", fn, (long long)n);
+    if (k <= 0) return fail(SDQ_ERR_INVALID, "%s: k (in features) must be >= 1; got %lld", fn, (long long)k);
+    if (k % 64 != 0)
+        return fail(SDQ_ERR_INVALID,
+                    "%s: k = %lld is not a multiple of the group size 64 (such weights stay dense)",
+                    fn, (long long)k);
+    if (n > INT32_MAX || k > INT32_MAX)
+        return fail(SDQ_ERR_INVALID, "%s: n and k must each be < 2^31", fn);
+    return SDQ_OK;
+}
+
+}  // namespace
+
+int set_error_message(int code, const char* msg) {
+    if (code == SDQ_OK) t_last_error.clear();
+    else t_last_error = msg ? msg : "";
+    return code;
+}
+
+int num_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    DevInfo& d = g_dev[dev];
+    if (!d.probed) check_device();
+    return d.sms > 0 ? d.sms : 148;
+}
+
+}  // namespace sdq
+
+using namespace sdq;
+
+extern "C" {
+
+const char* sdq_last_error(void) { return t_last_error.c_str(); }
+
+int sdq_abi_version(void) { return SDQ_ABI_VERSION; }
+
+size_t sdq_resident_bytes(int64_t n, int64_t k, int group_size, int bits, int sb_bytes) {
+    if (group_size <= 0) group_size = 64;
+    if (bits <= 0) bits = 4;
+    if (n < 0 || k <= 0 || k % group_size != 0 || (32 % bits) != 0 || sb_bytes <= 0) return 0;
+    const size_t packed = static_cast<size_t>(n) * static_cast<size_t>(k) * bits / 32 * 4;
+    const size_t sb = static_cast<size_t>(n) * static_cast<size_t>(k / group_size) * 2 * sb_bytes;
+    return packed + sb;
+}
+
+int sdq_quantize(const void* w, sdq_dtype w_dtype, int64_t n, int64_t k, int group_size, int bits,
+                 const char* mode, uint32_t* wq, void* scales, void* biases, sdq_dtype sb_dtype,
+                 void* stream) {
+    const char* fn = "sdq_quantize";
+    int rc;
+    if ((rc = check_qparams(group_size, bits, mode, fn))) return rc;
+    if ((rc = check_nk(n, k, fn))) return rc;
+    if (!w || !wq || !scales || !biases)
+        return fail(SDQ_ERR_INVALID, "%s: w, wq, scales and biases must be non-null", fn);
+    if (w_dtype != SDQ_F32 && w_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: weights must be f32 or bf16 (dtype %d)", fn, (int)w_dtype);
+    if (sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 only (dtype %d)", fn,
+                    (int)sb_dtype);
+    if (!aligned(w, w_dtype == SDQ_F32 ? 8 : 4) || !aligned(wq, 4) || !aligned(scales, 2) ||
+        !aligned(biases, 2))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (w needs %d bytes, wq 4, scales/biases 2)",
+                    fn, w_dtype == SDQ_F32 ? 8 : 4);
+    if ((rc = check_device())) return rc;
+    cudaError_t e = launch_quantize(w, w_dtype == SDQ_BF16, n, k, bits, wq, scales, biases,
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_quantize: kernel launch", e);
+    return ok();
+}
+
+int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases, sdq_dtype sb_dtype,
+                   int64_t n, int64_t k, int group_size, int bits, const char* mode, void* out,
+                   sdq_dtype out_dtype, void* stream) {
+    const char* fn = "sdq_dequantize";
+    int rc;
+    if ((rc = check_qparams(group_size, bits, mode, fn))) return rc;
+    if ((rc = check_nk(n, k, fn))) return rc;
+    if (!wq || !scales || !biases || !out)
+        return fail(SDQ_ERR_INVALID, "%s: wq, scales, biases and out must be non-null", fn);
+    if (sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 only", fn);
+    if (out_dtype != SDQ_BF16 && out_dtype != SDQ_F32)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: output must be bf16 or f32", fn);
+    if (!aligned(wq, 4) || !aligned(out, 16) || !aligned(scales, 2) || !aligned(biases, 2))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (out needs 16 bytes)", fn);
+    if ((rc = check_device())) return rc;
+    cudaError_t e = launch_dequantize(wq, scales, biases, n, k, bits, out, out_dtype == SDQ_F32,
+                                      static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_dequantize: kernel launch", e);
+    return ok();
+}
+
+int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
+                         const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n,
+                         int transpose, int group_size, int bits, const char* mode, const void* bias,
+                         void* y, sdq_dtype y_dtype, void* stream) {
+    const char* fn = "sdq_quantized_matmul";
+    int rc;
+    if ((rc = check_qparams(group_size, bits, mode, fn))) return rc;
+    if ((rc = check_nk(n, k, fn))) return rc;
+    if (m <= 0) return fail(SDQ_ERR_INVALID, "%s: m (rows of x) must be >= 1; got %lld", fn, (long long)m);
+    if (m > INT32_MAX) return fail(SDQ_ERR_INVALID, "%s: m must be < 2^31", fn);
+    if (!transpose)
+        return fail(SDQ_ERR_UNSUPPORTED,
+                    "%s: transpose=false is not supported (weights are [out, in]; pass true)", fn);
+    if (!x || !wq || !scales || !biases || !y)
+        return fail(SDQ_ERR_INVALID, "%s: x, wq, scales, biases and y must be non-null", fn);
+    if (x_dtype != SDQ_BF16 || y_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16", fn);
+    if (!aligned(x, 16) || !aligned(wq, 16) || !aligned(y, 2) || !aligned(scales, 2) ||
+        !aligned(biases, 2) || (bias && !aligned(bias, 2)))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
+    if ((rc = check_device())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (m <= kQmvMaxM && k <= kQmvMaxK) {
+        e = launch_qmv(x, (int)m, k, wq, scales, biases, n, bits, bias, y, st);
+        if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: small-M kernel", e);
+    } else {
+        const char* msg = nullptr;
+        e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y, st, &msg);
+        if (e != cudaSuccess) {
+            if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
+            return cuda_fail("sdq_quantized_matmul: tensor-core kernel", e);
+        }
+    }
+    return ok();
+}
+
+int sdq_device_status(void* stream) {
+    int rc;
+    if ((rc = check_device())) return rc;
+    unsigned int st = 0;
+    cudaError_t e = read_and_clear_status(&st, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_device_status", e);
+    if (st != 0) {
+        return fail(SDQ_ERR_TIMEOUT,
+                    "a device-side wait gave up (status bits 0x%x: 1 producer, 2 MMA, 4 dequant, "
+                    "8 epilogue); the kernel returned early and its output is incomplete",
+                    st);
+    }
+    return ok();
+}
+
+}  // extern "C"

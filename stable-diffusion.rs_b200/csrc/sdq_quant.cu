@@ -1,0 +1,202 @@
+// sdq_quant.cu -- affine group-wise quantise/pack and dequantise kernels.
+//
+// Quantise (replaces mlx_quantize behind QuantizedArray::quantize,
+// crates/sd-tensor/src/mlx.rs:1861-1911): one warp per group of 64 weights
+// along K; each lane owns two consecutive weights.  Group extrema come from a
+// 5-step warp-shuffle reduction under a total order (-0 < +0, NaN ignored), so
+// the result does not depend on the reduction tree.  The packed words are
+// assembled with two more shuffle steps and written coalesced.
+//
+// Dequantise (replaces mlx_dequantize behind QuantizedArray::dequantize,
+// mlx.rs:1918-1945): one thread per packed word, vector stores.
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "sdq_dequant.cuh"
+#include "sdq_internal.h"
+
+namespace sdq {
+
+__device__ __forceinline__ bool is_nan_f(float a) { return a != a; }
+
+// Same total order as the oracle's qmin / qmax.
+__device__ __forceinline__ float tmin(float a, float b) {
+    if (is_nan_f(a)) return b;
+    if (is_nan_f(b)) return a;
+    if (a < b) return a;
+    if (b < a) return b;
+    return (__float_as_uint(a) >> 31) ? a : b;
+}
+__device__ __forceinline__ float tmax(float a, float b) {
+    if (is_nan_f(a)) return b;
+    if (is_nan_f(b)) return a;
+    if (a > b) return a;
+    if (b > a) return b;
+    return (__float_as_uint(a) >> 31) ? b : a;
+}
+
+// Round-half-to-even binary32 -> bf16 bits, NaN -> 0x7fff (the oracle's rule).
+__device__ __forceinline__ uint32_t f32_to_bf16_rne(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fffu;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return u >> 16;
+}
+
+__device__ __forceinline__ uint32_t quant_one(float v, float s, float b, uint32_t qmax) {
+    if (s == 0.0f) return 0u;
+    const float t = __fdiv_rn(__fsub_rn(v, b), s);
+    const float r = rintf(t);
+    if (!(r > 0.0f)) return 0u;
+    if (r > (float)qmax) return qmax;
+    return (uint32_t)r;
+}
+
+template <int BITS, bool IN_BF16>
+__global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ w, int64_t n,
+                                                       int64_t k, uint32_t* __restrict__ wq,
+                                                       __nv_bfloat16* __restrict__ scales,
+                                                       __nv_bfloat16* __restrict__ biases) {
+    const int lane = threadIdx.x & 31;
+    const int64_t groups_per_row = k / 64;
+    const int64_t total = n * groups_per_row;
+    const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x / 32);
+    const int64_t wstride = (int64_t)gridDim.x * (blockDim.x / 32);
+    constexpr uint32_t qmax = (1u << BITS) - 1u;
+
+    for (int64_t gi = warp0; gi < total; gi += wstride) {
+        const int64_t row = gi / groups_per_row;
+        const int64_t g = gi - row * groups_per_row;
+        const int64_t e0 = row * k + g * 64 + 2 * lane;
+        float v0, v1;
+        if (IN_BF16) {
+            const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(
+                static_cast<const __nv_bfloat16*>(w) + e0));
+            v0 = bf16_bits_to_f32(pair & 0xFFFFu);
+            v1 = bf16_bits_to_f32(pair >> 16);
+        } else {
+            const float2 p = __ldg(reinterpret_cast<const float2*>(static_cast<const float*>(w) + e0));
+            v0 = p.x;
+            v1 = p.y;
+        }
+        float mn = tmin(v0, v1), mx = tmax(v0, v1);
+        // An all-NaN pair leaves NaN here; the oracle starts from +inf / -inf,
+        // which tmin / tmax reproduce when every value is NaN:
+        if (is_nan_f(mn)) { mn = __int_as_float(0x7f800000); mx = __int_as_float(0xff800000); }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            mn = tmin(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+            mx = tmax(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        }
+        const float scale = __fdiv_rn(__fsub_rn(mx, mn), (float)qmax);
+        const uint32_t sb = f32_to_bf16_rne(scale);
+        const uint32_t bb = f32_to_bf16_rne(mn);
+        const float s = bf16_bits_to_f32(sb);
+        const float b = bf16_bits_to_f32(bb);
+        const uint32_t q0 = quant_one(v0, s, b, qmax);
+        const uint32_t q1 = quant_one(v1, s, b, qmax);
+        const int64_t wbase = row * (k * BITS / 32) + g * (64 * BITS / 32);
+        if (BITS == 4) {
+            // lane l holds elements 2l, 2l+1: byte (l % 4) of word l / 4.
+            uint32_t v = (q0 | (q1 << 4)) << (8 * (lane & 3));
+            v |= __shfl_xor_sync(0xffffffffu, v, 1);
+            v |= __shfl_xor_sync(0xffffffffu, v, 2);
+            if ((lane & 3) == 0) wq[wbase + (lane >> 2)] = v;
+        } else {
+            // lane l holds elements 2l, 2l+1: half (l % 2) of word l / 2.
+            uint32_t v = (q0 | (q1 << 8)) << (16 * (lane & 1));
+            v |= __shfl_xor_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0) wq[wbase + (lane >> 1)] = v;
+        }
+        if (lane == 0) {
+            reinterpret_cast<uint16_t*>(scales)[gi] = (uint16_t)sb;
+            reinterpret_cast<uint16_t*>(biases)[gi] = (uint16_t)bb;
+        }
+    }
+}
+
+template <int BITS, bool OUT_F32>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ wq,
+                                                         const __nv_bfloat16* __restrict__ scales,
+                                                         const __nv_bfloat16* __restrict__ biases,
+                                                         int64_t n, int64_t k, void* __restrict__ out) {
+    constexpr int PER = 32 / BITS;  // elements per word
+    const int64_t words_per_row = k / PER;
+    const int64_t total = n * words_per_row;
+    const int64_t groups_per_row = k / 64;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / words_per_row;
+        const int64_t wi = i - row * words_per_row;
+        const int64_t g = row * groups_per_row + (wi * PER) / 64;
+        const uint32_t sbits = reinterpret_cast<const uint16_t*>(scales)[g];
+        const uint32_t bbits = reinterpret_cast<const uint16_t*>(biases)[g];
+        const uint32_t w = __ldg(wq + i);
+        const int64_t e0 = row * k + wi * PER;
+        if (BITS == 4) {
+            uint32_t o[4];
+            dq4_word_natural(w, sbits | (sbits << 16), bbits | (bbits << 16), o);
+            if (OUT_F32) {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + e0);
+                dst[0] = make_float4(__uint_as_float(o[0] << 16), __uint_as_float(o[0] & 0xFFFF0000u),
+                                     __uint_as_float(o[1] << 16), __uint_as_float(o[1] & 0xFFFF0000u));
+                dst[1] = make_float4(__uint_as_float(o[2] << 16), __uint_as_float(o[2] & 0xFFFF0000u),
+                                     __uint_as_float(o[3] << 16), __uint_as_float(o[3] & 0xFFFF0000u));
+            } else {
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + e0) =
+                    make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        } else {
+            uint32_t o[2];
+            dq8_word_natural(w, bf16_bits_to_f32(sbits), bf16_bits_to_f32(bbits), o);
+            if (OUT_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(out) + e0) =
+                    make_float4(__uint_as_float(o[0] << 16), __uint_as_float(o[0] & 0xFFFF0000u),
+                                __uint_as_float(o[1] << 16), __uint_as_float(o[1] & 0xFFFF0000u));
+            } else {
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + e0) = make_uint2(o[0], o[1]);
+            }
+        }
+    }
+}
+
+static int grid_for(int64_t work, int threads, int per_sm_blocks) {
+    const int64_t want = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)num_sms() * per_sm_blocks;
+    return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+cudaError_t launch_quantize(const void* w, bool w_bf16, int64_t n, int64_t k, int bits,
+                            uint32_t* wq, void* scales, void* biases, cudaStream_t st) {
+    const int64_t groups = n * (k / 64);
+    const int grid = grid_for(groups * 32, 256, 8);
+    auto* s = static_cast<__nv_bfloat16*>(scales);
+    auto* b = static_cast<__nv_bfloat16*>(biases);
+    if (bits == 4) {
+        if (w_bf16) quantize_kernel<4, true><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+        else quantize_kernel<4, false><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+    } else {
+        if (w_bf16) quantize_kernel<8, true><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+        else quantize_kernel<8, false><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, int64_t n,
+                              int64_t k, int bits, void* out, bool out_f32, cudaStream_t st) {
+    const int64_t words = n * k * bits / 32;
+    const int grid = grid_for(words, 256, 8);
+    auto* s = static_cast<const __nv_bfloat16*>(scales);
+    auto* b = static_cast<const __nv_bfloat16*>(biases);
+    if (bits == 4) {
+        if (out_f32) dequantize_kernel<4, true><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+        else dequantize_kernel<4, false><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+    } else {
+        if (out_f32) dequantize_kernel<8, true><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+        else dequantize_kernel<8, false><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace sdq

@@ -1,0 +1,207 @@
+"""sdq -- B200-native affine group-wise quantised linear (host-side mirror).
+
+This package mirrors the reference's `sd-tensor` seam for quantised weights,
+``QuantizedArray::{quantize, dequantize, matmul, resident_bytes}``
+(andreinknv/stable-diffusion.rs, crates/sd-tensor/src/mlx.rs:1846-1986), over
+the C ABI of ``libsdq.so`` (include/sdq.h).  Tensors are torch CUDA tensors used
+purely as device memory; every computation is a libsdq kernel.  There is no
+CPU fallback: on a machine without an sm_100 device the calls raise
+:class:`SdqError`.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from ._abi import (SDQ_BF16, SDQ_ERR_CUDA, SDQ_ERR_INVALID, SDQ_ERR_NCCL, SDQ_ERR_TIMEOUT,
+                   SDQ_ERR_UNSUPPORTED, SDQ_F16, SDQ_F32, SDQ_OK, SdqError, check, last_error, lib)
+
+__all__ = [
+    "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "resident_bytes",
+    "device_status", "Comm", "quantized_matmul_sharded", "GROUP_SIZE", "MODE",
+    "SDQ_OK", "SDQ_ERR_INVALID", "SDQ_ERR_UNSUPPORTED", "SDQ_ERR_CUDA", "SDQ_ERR_TIMEOUT",
+    "SDQ_ERR_NCCL",
+]
+
+#: MLX's default group size (crates/sd-models/src/mlx/quantized.rs:45-46).
+GROUP_SIZE = 64
+#: The quantisation mode the reference always asks for (mlx.rs:1830-1832).
+MODE = "affine"
+
+_DT = {torch.float32: SDQ_F32, torch.bfloat16: SDQ_BF16, torch.float16: SDQ_F16}
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise SdqError(SDQ_ERR_UNSUPPORTED, f"dtype {t.dtype} has no libsdq code")
+    return _DT[t.dtype]
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise SdqError(SDQ_ERR_INVALID, "libsdq takes device tensors (no CPU fallback)")
+        if t is not None and not t.is_contiguous():
+            raise SdqError(SDQ_ERR_INVALID, "libsdq takes contiguous row-major tensors")
+
+
+def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None):
+    """``mlx_quantize`` replacement: w [n, k] f32/bf16 -> (wq u32 [n, k*bits/32] as int32,
+    scales bf16 [n, k/64], biases bf16 [n, k/64])."""
+    _need_cuda(w)
+    if w.dim() != 2:
+        raise SdqError(SDQ_ERR_INVALID, f"quantize wants a 2-D weight, got shape {tuple(w.shape)}")
+    n, k = w.shape
+    if bits not in (4, 8) or k % GROUP_SIZE != 0:
+        # Let the library produce the canonical message and code.
+        dummy = torch.empty(1, device=w.device, dtype=torch.int32)
+        check(lib().sdq_quantize(_ptr(w), _dt(w), n, k, group_size, bits, MODE.encode(), _ptr(dummy),
+                                 _ptr(dummy), _ptr(dummy), SDQ_BF16, _stream(stream)))
+    wq = torch.empty((n, k * bits // 32), device=w.device, dtype=torch.int32)
+    s = torch.empty((n, k // GROUP_SIZE), device=w.device, dtype=torch.bfloat16)
+    b = torch.empty_like(s)
+    check(lib().sdq_quantize(_ptr(w), _dt(w), n, k, group_size, bits, MODE.encode(), _ptr(wq), _ptr(s),
+                             _ptr(b), SDQ_BF16, _stream(stream)))
+    return wq, s, b
+
+
+def dequantize(wq, scales, biases, group_size: int = GROUP_SIZE, bits: int = 4,
+               out_dtype=torch.bfloat16, stream=None) -> torch.Tensor:
+    """``mlx_dequantize`` replacement: reconstruct [n, k] (one rounding of s*q + b)."""
+    _need_cuda(wq, scales, biases)
+    n = wq.shape[0]
+    k = wq.shape[1] * 32 // bits
+    out = torch.empty((n, k), device=wq.device, dtype=out_dtype)
+    check(lib().sdq_dequantize(_ptr(wq), _ptr(scales), _ptr(biases), _dt(scales), n, k, group_size, bits,
+                               MODE.encode(), _ptr(out), _dt(out), _stream(stream)))
+    return out
+
+
+def quantized_matmul(x: torch.Tensor, wq, scales, biases, group_size: int = GROUP_SIZE, bits: int = 4,
+                     bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                     stream=None) -> torch.Tensor:
+    """``mlx_quantized_matmul`` replacement (transpose=true): x [..., k] -> [..., n].
+
+    A 3-D ``x`` ([b, s, k]) is flattened to M = b*s rows, as MLX does."""
+    _need_cuda(x, wq, scales, biases, bias, out)
+    lead = x.shape[:-1]
+    k = x.shape[-1]
+    m = 1
+    for d in lead:
+        m *= d
+    n = wq.shape[0]
+    if out is None:
+        out = torch.empty((*lead, n), device=x.device, dtype=torch.bfloat16)
+    check(lib().sdq_quantized_matmul(_ptr(x), _dt(x), m, k, _ptr(wq), _ptr(scales), _ptr(biases),
+                                     _dt(scales), n, 1, group_size, bits, MODE.encode(), _ptr(bias),
+                                     _ptr(out), _dt(out), _stream(stream)))
+    return out
+
+
+def resident_bytes(n: int, k: int, bits: int, group_size: int = GROUP_SIZE, sb_bytes: int = 4) -> int:
+    """Packed words plus scales and biases; ``sb_bytes=4`` counts them as the reference does
+    (mlx.rs:1981-1985), ``sb_bytes=2`` is what this library actually stores."""
+    return int(lib().sdq_resident_bytes(n, k, group_size, bits, sb_bytes))
+
+
+def device_status(stream=None) -> None:
+    """Raise :class:`SdqError` (SDQ_ERR_TIMEOUT) if a kernel's bounded wait gave up."""
+    check(lib().sdq_device_status(_stream(stream)))
+
+
+@dataclass
+class QuantizedArray:
+    """A weight held quantised at rest (mlx.rs:1846-1854): packed ``weight`` (u32 words,
+    ``32 / bits`` values each), ``scales``, ``biases``, ``group_size``, ``bits``.
+
+    ``bits`` and ``group_size`` must match what the weight was quantised with; nothing in the
+    tensors records them (mlx.rs:1842-1845)."""
+    weight: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    group_size: int
+    bits: int
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None):
+        """``[out, in]`` in, packed ``[out, in * bits / 32]`` out (mlx.rs:1861)."""
+        wq, s, b = quantize(w, group_size, bits, stream)
+        return cls(wq, s, b, group_size, bits)
+
+    def dequantize(self, out_dtype=torch.bfloat16, stream=None) -> torch.Tensor:
+        """Reconstruct the dense array -- for tests, not the hot path (mlx.rs:1913-1918)."""
+        return dequantize(self.weight, self.scales, self.biases, self.group_size, self.bits,
+                          out_dtype, stream)
+
+    def matmul(self, x: torch.Tensor, bias: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """``x @ weight.T``, dequantising inside the kernel (mlx.rs:1947-1975)."""
+        return quantized_matmul(x, self.weight, self.scales, self.biases, self.group_size, self.bits,
+                                bias=bias, stream=stream)
+
+    def resident_bytes(self) -> int:
+        """Bytes this weight occupies, counted as the reference does (4 bytes per scale)."""
+        packed = self.weight.numel() * 4
+        sb = (self.scales.numel() + self.biases.numel()) * 4
+        return packed + sb
+
+    @property
+    def shape(self):
+        return (self.weight.shape[0], self.weight.shape[1] * 32 // self.bits)
+
+
+class Comm:
+    """A libsdq-owned NCCL communicator for the column-sharded linear."""
+
+    def __init__(self, unique_id: bytes, world: int, rank: int):
+        if len(unique_id) != 128:
+            raise SdqError(SDQ_ERR_INVALID, "NCCL unique id must be 128 bytes")
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = ctypes.c_void_p()
+        check(lib().sdq_comm_init(buf, world, rank, ctypes.byref(h)))
+        self.handle = h
+        self.world = world
+        self.rank = rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        check(lib().sdq_comm_unique_id(buf))
+        return bytes(buf)
+
+    def destroy(self) -> None:
+        if self.handle:
+            check(lib().sdq_comm_destroy(self.handle))
+            self.handle = None
+
+
+def quantized_matmul_sharded(x, wq, scales, biases, comm: Comm, group_size: int = GROUP_SIZE,
+                             bits: int = 4, bias=None, y_shards=None, out=None, permute: bool = True,
+                             stream=None):
+    """Column-sharded quantised linear: local rows of W -> all-gathered Y [m, world * n_local].
+
+    Returns ``(out, y_shards)``; ``out`` is None when ``permute`` is False (the caller then
+    reads the blocked [world, m, n_local] layout from ``y_shards``)."""
+    _need_cuda(x, wq, scales, biases, bias)
+    m, k = x.reshape(-1, x.shape[-1]).shape
+    nl = wq.shape[0]
+    if y_shards is None:
+        y_shards = torch.empty((comm.world, m, nl), device=x.device, dtype=torch.bfloat16)
+    if permute and out is None:
+        out = torch.empty((m, comm.world * nl), device=x.device, dtype=torch.bfloat16)
+    check(lib().sdq_quantized_matmul_sharded(
+        _ptr(x), _dt(x), m, k, _ptr(wq), _ptr(scales), _ptr(biases), _dt(scales), nl, group_size, bits,
+        _ptr(bias), _ptr(y_shards), _ptr(out) if permute else None, SDQ_BF16, comm.handle,
+        _stream(stream)))
+    return (out if permute else None), y_shards
