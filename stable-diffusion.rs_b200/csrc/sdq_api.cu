@@ -201,7 +201,10 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
     if ((rc = check_device())) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (m <= kQmvMaxM && k <= kQmvMaxK) {
+    // The small-M kernel streams 16 packed words per row per step: 128 k at 4
+    // bits, 64 k at 8 bits.  Other shapes go to the tensor-core kernel.
+    const bool qmv_shape = k <= kQmvMaxK && (bits == 8 || k % 128 == 0);
+    if (m <= kQmvMaxM && qmv_shape) {
         e = launch_qmv(x, (int)m, k, wq, scales, biases, n, bits, bias, y, st);
         if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: small-M kernel", e);
     } else {

@@ -17,11 +17,13 @@
 // a third of the tensor-core time.  One quantisation group (64 k) is exactly
 // one pipeline stage, so each stage needs one scale and one bias per row.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: X tile + packed W tile per stage (no multicast)
 //   warp 1      TMEM allocator and MMA issuer
-//   warps 4-7   dequant: thread r owns feature row r of the tile
-//   warps 8-11  epilogue: TMEM -> registers -> (+bias) -> bf16 -> global
+//   warps 4-11  dequant, two warpgroups taking alternate stages (so that one
+//               group's TMEM-store and barrier latency hides behind the
+//               other's unpacking); thread r of a group owns feature row r
+//   warps 12-15 epilogue: TMEM -> registers -> (+bias) -> bf16 -> global
 // Every mbarrier wait is bounded (2 s); on expiry the kernel records a status
 // bit, drains its own copies and MMAs, frees TMEM and returns.
 #include <cstdint>
@@ -56,10 +58,11 @@ struct TcCfg {
     static constexpr int SMEM_BYTES = 1024 + STAGES * (X_STAGE + W_STAGE) + 256;
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N must be 16..256, step 16");
     static_assert(STAGES * 32 <= 256, "A slots must fit beside the accumulator");
+    static_assert(STAGES % 2 == 0, "the two dequant warpgroups alternate stages");
 };
 
 template <int BITS, int BT, int STAGES>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const uint16_t* __restrict__ scales, const uint16_t* __restrict__ biases,
                   const uint16_t* __restrict__ bias, uint16_t* __restrict__ y, int M, int N, int K) {
@@ -172,9 +175,10 @@ __global__ void __launch_bounds__(384, 1)
                 mbar_wait_drain(drain, 0);
             }
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------------ dequant
-        const int r = threadIdx.x - 128;                      // feature row in the tile
+        const int grp_id = (warp - 4) >> 2;                   // takes stages with it % 2 == grp_id
+        const int r = (threadIdx.x - 128) & 127;              // feature row in the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const int G = K / 64;
         int it = 0;
@@ -187,6 +191,7 @@ __global__ void __launch_bounds__(384, 1)
             const uint16_t* srow = scales + (int64_t)(valid ? row : 0) * G;
             const uint16_t* brow = biases + (int64_t)(valid ? row : 0) * G;
             for (int kt = 0; kt < KT; ++kt, ++it) {
+                if ((it & 1) != grp_id) continue;
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1;
                 const uint32_t sb = valid ? (uint32_t)__ldg(srow + kt) : 0u;
@@ -231,7 +236,7 @@ __global__ void __launch_bounds__(384, 1)
                 mbar_arrive(afull + s);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 12) {
         // ------------------------------------------------------------ epilogue
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         int tc = 0;
@@ -338,7 +343,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     }
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    qmm_tc_kernel<BITS, BT, STAGES><<<grid, 384, C::SMEM_BYTES, st>>>(
+    qmm_tc_kernel<BITS, BT, STAGES><<<grid, 512, C::SMEM_BYTES, st>>>(
         tmX, tmW, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
         static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
     return cudaGetLastError();

@@ -41,21 +41,11 @@ struct QmvCfg {
     static constexpr int CH = RPL / 4;                // uint4 chunks of X fragments per lane
 };
 
-// Element offsets (within a block) of the two halves of fragment register r of
-// quad lane t.  W4: word w = r / 4 of the lane's 16 bytes, nibble pair (j, j+4).
-// W8: word w = r / 2, byte pair (2j, 2j+1).
-template <int BITS>
-__device__ __forceinline__ void frag_k(int r, int t, int& ka, int& kb) {
-    if (BITS == 4) {
-        const int w = r >> 2, j = r & 3;
-        ka = 32 * t + 8 * w + j;
-        kb = ka + 4;
-    } else {
-        const int w = r >> 1, j = r & 1;
-        ka = 16 * t + 4 * w + 2 * j;
-        kb = ka + 1;
-    }
-}
+// Fragment register r of quad lane t holds two k of the block (lo, hi half):
+//   W4: word w = r / 4 of the lane's 16 bytes, nibbles (j, j+4), j = r % 4:
+//       k = 32 t + 8 w + j and k + 4;
+//   W8: word w = r / 2, bytes (2j, 2j+1), j = r % 2: k = 16 t + 4 w + 2 j and k + 1.
+// The activation fragments are staged in shared memory in the same order.
 
 __device__ __forceinline__ uint4 ld_stream_v4(const uint32_t* p) {
     uint4 v;
@@ -141,24 +131,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int p = 0; p < kRing; ++p) load_item(p, ring[p]);
 
-    // Stage X (zero-padded to 8 rows) in fragment order.
+    // Stage X (zero-padded to 8 rows) in fragment order: one 16-byte load of 8
+    // consecutive k and one 16-byte shared store per thread and step.  An aligned
+    // run of 8 k lands in the four components of one lane's uint4 chunk
+    // (W4: halves (j, j+4); W8: natural pairs).
     {
-        const int regs = nblk * C::CH * 32 * 4;
-        uint32_t* xs32 = reinterpret_cast<uint32_t*>(xs);
-        for (int i = threadIdx.x; i < regs; i += kThreads) {
-            const int comp = i & 3;
-            const int ln = (i >> 2) & 31;
-            const int c = (i >> 7) % C::CH;
-            const int blk = (i >> 7) / C::CH;
-            const int tok = ln >> 2, tt = ln & 3;
-            int ka, kb;
-            frag_k<BITS>(4 * c + comp, tt, ka, kb);
-            uint32_t v = 0;
+        const int chunks_per_row = k / 8;
+        const int total_chunks = 8 * chunks_per_row;
+        for (int i = threadIdx.x; i < total_chunks; i += kThreads) {
+            const int tok = i / chunks_per_row;
+            const int kc = (i - tok * chunks_per_row) * 8;       // first k of the run
+            const int blk = kc / C::KB;
+            const int kk = kc - blk * C::KB;                     // offset inside the block
+            int t, c;
+            if (BITS == 4) { t = kk >> 5; c = (kk & 31) >> 3; }
+            else { t = kk >> 4; c = (kk & 15) >> 3; }
+            uint4 v = make_uint4(0, 0, 0, 0);
             if (tok < m) {
-                const uint16_t* row = x + (int64_t)tok * k + (int64_t)blk * C::KB;
-                v = (uint32_t)row[ka] | ((uint32_t)row[kb] << 16);
+                const uint4 raw = *reinterpret_cast<const uint4*>(x + (int64_t)tok * k + kc);
+                if (BITS == 4) {
+                    // raw = e0e1 e2e3 e4e5 e6e7 -> (e0,e4) (e1,e5) (e2,e6) (e3,e7)
+                    v.x = prmt(raw.x, raw.z, 0x5410u);
+                    v.y = prmt(raw.x, raw.z, 0x7632u);
+                    v.z = prmt(raw.y, raw.w, 0x5410u);
+                    v.w = prmt(raw.y, raw.w, 0x7632u);
+                } else {
+                    v = raw;
+                }
             }
-            xs32[i] = v;
+            xs[((int64_t)blk * C::CH + c) * 32 + tok * 4 + t] = v;
         }
     }
     __syncthreads();

@@ -20,7 +20,7 @@ from ._abi import (SDQ_BF16, SDQ_ERR_CUDA, SDQ_ERR_INVALID, SDQ_ERR_NCCL, SDQ_ER
 
 __all__ = [
     "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "resident_bytes",
-    "device_status", "Comm", "quantized_matmul_sharded", "GROUP_SIZE", "MODE",
+    "device_status", "Comm", "quantized_matmul_sharded", "shard_rows", "unshard", "GROUP_SIZE", "MODE",
     "SDQ_OK", "SDQ_ERR_INVALID", "SDQ_ERR_UNSUPPORTED", "SDQ_ERR_CUDA", "SDQ_ERR_TIMEOUT",
     "SDQ_ERR_NCCL",
 ]
@@ -184,6 +184,24 @@ class Comm:
         if self.handle:
             check(lib().sdq_comm_destroy(self.handle))
             self.handle = None
+
+
+def shard_rows(n_total: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [start, stop) of an [n_total, k] weight held by `rank` in the column-sharded
+    linear; n_total must divide evenly (every rank runs the same kernel shape)."""
+    if n_total % world != 0:
+        raise SdqError(SDQ_ERR_INVALID, f"{n_total} output features do not split over {world} ranks")
+    nl = n_total // world
+    return rank * nl, (rank + 1) * nl
+
+
+def unshard(y_shards):
+    """The permute the library applies after the all-gather: [world, m, n_local] -> [m, world*n_local]
+    (host-side statement of the same index map, for arrays or tensors)."""
+    w, m, nl = y_shards.shape
+    if hasattr(y_shards, "permute"):
+        return y_shards.permute(1, 0, 2).reshape(m, w * nl)
+    return y_shards.transpose(1, 0, 2).reshape(m, w * nl)
 
 
 def quantized_matmul_sharded(x, wq, scales, biases, comm: Comm, group_size: int = GROUP_SIZE,
