@@ -94,9 +94,10 @@ int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases,
  * (mlx.rs:386-397) as called by QuantizedArray::matmul (mlx.rs:1952-1975) and,
  * with `bias`, the separate `y.add(bias)` of quantized::linear
  * (crates/sd-models/src/mlx/quantized.rs:314-317).  `transpose` must be true
- * (the reference always passes true).  m >= 1.  m <= 8 with k <= 12288 runs
- * the HBM-streaming small-M kernel; anything else runs the tcgen05
- * tensor-core kernel.  x and wq must be 16-byte aligned.
+ * (the reference always passes true).  m >= 1.  Every shape runs the tcgen05
+ * tensor-core kernel; the token tile (16 / 64 / 128 / 256 rows of x) follows
+ * m, and for m <= 16 the activations stay resident in shared memory while the
+ * packed weight streams from HBM.  x and wq must be 16-byte aligned.
  */
 int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                          const uint32_t* wq, const void* scales, const void* biases,

@@ -199,21 +199,12 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
         !aligned(biases, 2) || (bias && !aligned(bias, 2)))
         return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
     if ((rc = check_device())) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e;
-    // The small-M kernel streams 16 packed words per row per step: 128 k at 4
-    // bits, 64 k at 8 bits.  Other shapes go to the tensor-core kernel.
-    const bool qmv_shape = k <= kQmvMaxK && (bits == 8 || k % 128 == 0);
-    if (m <= kQmvMaxM && qmv_shape) {
-        e = launch_qmv(x, (int)m, k, wq, scales, biases, n, bits, bias, y, st);
-        if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: small-M kernel", e);
-    } else {
-        const char* msg = nullptr;
-        e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y, st, &msg);
-        if (e != cudaSuccess) {
-            if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
-            return cuda_fail("sdq_quantized_matmul: tensor-core kernel", e);
-        }
+    const char* msg = nullptr;
+    const cudaError_t e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y,
+                                        static_cast<cudaStream_t>(stream), &msg);
+    if (e != cudaSuccess) {
+        if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
+        return cuda_fail("sdq_quantized_matmul: tensor-core kernel", e);
     }
     return ok();
 }

@@ -15,14 +15,7 @@ cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void
                               int64_t n, int64_t k, int bits, void* out, bool out_f32,
                               cudaStream_t st);
 
-// Small-M path (1 <= m <= kQmvMaxM, k <= kQmvMaxK): HBM-streaming kernel.
-constexpr int kQmvMaxM = 8;
-constexpr int64_t kQmvMaxK = 12288;
-cudaError_t launch_qmv(const void* x, int m, int64_t k, const uint32_t* wq, const void* scales,
-                       const void* biases, int64_t n, int bits, const void* bias, void* y,
-                       cudaStream_t st);
-
-// Large-M path: TMA + tcgen05 (TMEM) tensor-core kernel.  Returns a CUDA error
+// Quantised matmul on the tensor cores (TMA + tcgen05 / TMEM), every M.  Returns a CUDA error
 // or cudaSuccess; `msg` receives a description when tensor-map encoding fails.
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,

@@ -79,6 +79,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Warp-collective form of mbar_wait for warps that go on to issue
+// .sync.aligned tcgen05 instructions (tcgen05.st / ld / wait::*): each lane
+// waits (and so acquires) on its own, then the warp votes, which also
+// reconverges it.  Lanes leave a spin loop at different iterations; an
+// .aligned instruction issued by a diverged warp is undefined (in practice
+// parts of a TMEM store were not there when the MMA read them).  The vote
+// also keeps the give-up decision uniform across the warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               unsigned int* status, unsigned int status_bit) {
+    const bool ok = mbar_wait(bar, parity, abort, status, status_bit);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait used only while draining after an abort: ignores the abort flag.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
     const unsigned long long t0 = globaltimer();
@@ -172,6 +185,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
         "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
+}
+// Warp-collective: lane i reads 16 consecutive 32-bit columns of TMEM lane (taddr.lane + i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA and the tensor core's shared-memory operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 // Warp-collective: lane i reads 32 consecutive 32-bit columns of TMEM lane (taddr.lane + i).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -1,4 +1,4 @@
-// sdq_qmm_tc.cu -- large-M quantised matmul on the 5th-generation tensor cores.
+// sdq_qmm_tc.cu -- quantised matmul on the 5th-generation tensor cores.
 //
 // Y[m, n] = X[m, k] . dequant(Wq, S, B)[n, k]^T, the op behind
 // QuantizedArray::matmul (crates/sd-tensor/src/mlx.rs:1947-1975) that every
@@ -6,27 +6,40 @@
 //
 // The kernel computes the transposed tile D[f, t] = W_dq[f, :] . X[t, :]^T with
 //   * A = the dequantised weight tile, 128 features x 64 k, written straight
-//     into TENSOR MEMORY by a dequant warpgroup (tcgen05.st) -- it never
+//     into TENSOR MEMORY by the dequant warpgroups (tcgen05.st) -- it never
 //     passes through shared memory;
-//   * B = the activation tile, BT tokens x 64 k bf16, loaded by TMA with
-//     128-byte swizzle into shared memory;
+//   * B = the activation tile, BT tokens x 64 k bf16 in shared memory with
+//     128-byte swizzle (loaded per step by TMA, or -- for BT = 16 when X fits
+//     -- staged once at kernel start and kept resident);
 //   * D = 128 x BT f32 accumulator in TMEM (tcgen05.mma kind::f16, issued by
 //     one thread).
-// With tokens on the MMA N side (up to 256), every dequantised weight element
-// feeds BT = 256 multiply-adds, which keeps the CUDA-core unpack work at about
-// a third of the tensor-core time.  One quantisation group (64 k) is exactly
-// one pipeline stage, so each stage needs one scale and one bias per row.
+// With tokens on the MMA N side, every dequantised weight element feeds BT
+// multiply-adds; one quantisation group (64 k) is one pipeline step, so each
+// step needs one scale and one bias per row.
 //
-// Warp roles (512 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer: X tile + packed W tile per stage (no multicast)
+// Three rings decouple the producers from the consumer:
+//   X ring  (SX slots in smem)  TMA producer -> MMA
+//   W ring  (SW slots in smem)  TMA producer -> dequant (packed words only: deep)
+//   A ring  (SA slots in TMEM)  dequant      -> MMA
+// so the weight stream and its unpacking run many steps ahead of the MMAs.
+//
+// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer of the X ring (idle when X is resident)
 //   warp 1      TMEM allocator and MMA issuer
-//   warps 4-11  dequant, two warpgroups taking alternate stages (so that one
-//               group's TMEM-store and barrier latency hides behind the
-//               other's unpacking); thread r of a group owns feature row r
-//   warps 12-15 epilogue: TMEM -> registers -> (+bias) -> bf16 -> global
+//   warp 2      TMA producer of the W ring
+//   warps 4-7   dequant warpgroup; thread r owns feature row r of the tile
+//   warps 8-11  epilogue: TMEM -> registers -> (+bias) -> bf16 -> global
+// Exactly one warp stores to each TMEM sub-partition (lanes 32w..32w+31).  With
+// two dequant warpgroups taking alternate steps -- two warps of one SM
+// sub-partition storing different columns of the same TMEM lanes at the same
+// time -- the MMAs occasionally read A columns that one warp's completed,
+// waited-for store had not yet made visible; one storing warp per
+// sub-partition never showed it, and costs nothing here (the single MMA-issuing
+// thread, not the unpacking, bounds the step rate).
 // Every mbarrier wait is bounded (2 s); on expiry the kernel records a status
 // bit, drains its own copies and MMAs, frees TMEM and returns.
 #include <cstdint>
+#include <cstring>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -43,42 +56,66 @@ __device__ unsigned int g_tc_status = 0;
 
 namespace {
 
-template <int BITS, int BT, int STAGES>
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 struct TcCfg {
     static constexpr int BF = 128;                         // features per tile = MMA M
-    static constexpr int BK = 64;                          // k per stage = one group
+    static constexpr int BK = 64;                          // k per step = one group
     static constexpr int X_STAGE = BT * BK * 2;            // bytes, 128 B per token row
     static constexpr int W_ROW = BK * BITS / 8;            // packed bytes per feature row
     static constexpr int W_STAGE = BF * W_ROW;
-    static constexpr int TX_BYTES = X_STAGE + W_STAGE;
-    static constexpr int W_WORDS = BK * BITS / 32;         // packed words per row per stage
+    static constexpr int W_WORDS = BK * BITS / 32;         // packed words per row per step
     static constexpr uint32_t D_COL = 0;                   // accumulator columns [0, BT)
-    static constexpr uint32_t A_COL = 256;                 // A slots: 32 columns each
+    static constexpr uint32_t A_COL = BT < 32 ? 32 : BT;   // A slots: 32 columns each
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * (X_STAGE + W_STAGE) + 256;
+    static constexpr int RING_BYTES = (XRES ? 0 : SX * X_STAGE) + SW * W_STAGE;
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N must be 16..256, step 16");
-    static_assert(STAGES * 32 <= 256, "A slots must fit beside the accumulator");
-    static_assert(STAGES % 2 == 0, "the two dequant warpgroups alternate stages");
+    static_assert(A_COL + 32 * SA <= TMEM_COLS, "A slots must fit beside the accumulator");
+    static_assert(!XRES || BT == 16, "resident activations only for the 16-token tile");
+    static_assert(XRES || SX <= SA, "an X slot is released through the done barrier of its step");
 };
 
-template <int BITS, int BT, int STAGES>
-__global__ void __launch_bounds__(512, 1)
+// Bytes of dynamic shared memory a configuration needs for a given K.
+template <class C, bool XRES, int BT>
+size_t smem_bytes(int64_t k) {
+    size_t b = 1024 + C::RING_BYTES + 1024;   // alignment slack, rings, barriers
+    if (XRES) b += (size_t)(k / 64) * (BT * 128);
+    return b;
+}
+
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
+__global__ void __launch_bounds__(384, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                  const uint16_t* __restrict__ scales, const uint16_t* __restrict__ biases,
-                  const uint16_t* __restrict__ bias, uint16_t* __restrict__ y, int M, int N, int K) {
-    using C = TcCfg<BITS, BT, STAGES>;
+                  const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
+                  const uint16_t* __restrict__ biases, const uint16_t* __restrict__ bias,
+                  uint16_t* __restrict__ y, int M, int N, int K) {
+    using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint8_t* sX = smem;                                  // STAGES x X_STAGE (1024-aligned)
-    uint8_t* sW = smem + STAGES * C::X_STAGE;            // STAGES x W_STAGE
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sW + STAGES * C::W_STAGE);
-    uint64_t* full = bars;                // TMA landed (X + W)            count 1 + tx
-    uint64_t* afull = bars + STAGES;      // A slot written               count 128
-    uint64_t* done = bars + 2 * STAGES;   // MMAs of the stage finished    count 1 (commit)
-    uint64_t* dfull = bars + 3 * STAGES;  // accumulator complete          count 1 (commit)
-    uint64_t* dempty = dfull + 1;         // accumulator drained           count 128
-    uint64_t* drain = dfull + 2;          // abort drain of the MMA pipe   count 1 (commit)
+    const int KT = K / C::BK;
+    // Layout: [X ring or resident X (1024-aligned tiles)] [W ring] [barriers].
+    uint8_t* sX = smem;
+    const size_t x_bytes = XRES ? (size_t)KT * C::X_STAGE : (size_t)SX * C::X_STAGE;
+    uint8_t* sW = smem + x_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sW + SW * C::W_STAGE);
+    // Step s uses X slot s % SX, W slot s % SW and A slot / barrier pair s % SA.
+    //   xfull[x]   X landed                               count 1 + tx
+    //   xempty[x]  the MMAs that read X slot x finished   count 1 (commit)
+    //   wfull[w]   packed W landed                       count 1 + tx
+    //   wempty[w]  the dequant group read W slot w        count 128
+    //   ready[a]   A slot written                         count 128
+    //   done[a]    the MMAs that read A slot a finished   count 1 (commit)
+    // The MMA thread itself waits on xfull: the tensor core's shared-memory reads
+    // are ordered after the bulk copy through that wait.
+    uint64_t* xfull = bars;
+    uint64_t* xempty = xfull + SX;
+    uint64_t* wfull = xempty + SX;
+    uint64_t* wempty = wfull + SW;
+    uint64_t* ready = wempty + SW;
+    uint64_t* done = ready + SA;
+    uint64_t* dfull = done + SA;             // accumulator complete       count 1 (commit)
+    uint64_t* dempty = dfull + 1;            // accumulator drained        count 128
+    uint64_t* drain = dfull + 2;             // abort drain of the MMA pipe
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     unsigned int* status = &g_tc_status;
@@ -87,22 +124,45 @@ __global__ void __launch_bounds__(512, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full + s, 1);
-            mbar_init(afull + s, 128);
-            mbar_init(done + s, 1);
-        }
+        for (int i = 0; i < SX; ++i) { mbar_init(xfull + i, 1); mbar_init(xempty + i, 1); }
+        for (int i = 0; i < SW; ++i) { mbar_init(wfull + i, 1); mbar_init(wempty + i, 128); }
+        for (int i = 0; i < SA; ++i) { mbar_init(ready + i, 128); mbar_init(done + i, 1); }
         mbar_init(dfull, 1);
         mbar_init(dempty, 128);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&tmX);
+        if (!XRES) tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
+    }
+    if (XRES) {
+        // Stage all of X (16 rows, zero beyond M) once, in the 128B-swizzled K-major
+        // layout the MMA reads, with k permuted inside each 8-element run to
+        // (0,4,1,5,2,6,3,7) -- the order in which the dequant's nibble unpack emits
+        // weight pairs (see dq4_word_interleaved).  8-bit weights unpack in natural
+        // order, so their activations stay natural.
+        const int chunks = KT * 16 * 8;
+        for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+            const int c = i & 7, row = (i >> 3) & 15, kt = i >> 7;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row < M) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(xg + (int64_t)row * K + kt * 64 + c * 8);
+                if (BITS == 4) {
+                    v.x = prmt(raw.x, raw.z, 0x5410u);
+                    v.y = prmt(raw.x, raw.z, 0x7632u);
+                    v.z = prmt(raw.y, raw.w, 0x5410u);
+                    v.w = prmt(raw.y, raw.w, 0x7632u);
+                } else {
+                    v = raw;
+                }
+            }
+            *reinterpret_cast<uint4*>(sX + (size_t)kt * C::X_STAGE + row * 128 + ((c ^ (row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
     }
     tc_fence_before();
     __syncthreads();
@@ -112,60 +172,81 @@ __global__ void __launch_bounds__(512, 1)
     const int nft = (N + C::BF - 1) / C::BF;
     const int ntt = (M + BT - 1) / BT;
     const int ntiles = nft * ntt;
-    const int KT = K / C::BK;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            int it = 0;
-            int last_phase[STAGES];
-            bool issued[STAGES];
-            for (int s = 0; s < STAGES; ++s) { issued[s] = false; last_phase[s] = 0; }
+        // ------------------------------------------------------------ X producer
+        // Step s's X lands on xfull[s % SX]; the slot is reused by step s + SX once the
+        // MMAs of step s are done.
+        if (lane == 0 && !XRES) {
+            int it = 0, last_it = -1;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-                const int tt = tile / nft, ft = tile - tt * nft;
+                const int tt = tile / nft;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(done + s, ph ^ 1, abort_flag, status, 1u)) { ok = false; break; }
-                    mbar_arrive_expect_tx(full + s, C::TX_BYTES);
-                    tma_load_2d(sX + s * C::X_STAGE, &tmX, full + s, kt * C::BK, tt * BT);
-                    tma_load_2d(sW + s * C::W_STAGE, &tmW, full + s, kt * C::W_WORDS, ft * C::BF);
-                    issued[s] = true;
-                    last_phase[s] = (int)ph;
+                    if (!mbar_wait(xempty + it % SX, ((it / SX) & 1) ^ 1, abort_flag, status, 1u)) { ok = false; break; }
+                    uint64_t* bar = xfull + it % SX;
+                    mbar_arrive_expect_tx(bar, C::X_STAGE);
+                    tma_load_2d(sX + (it % SX) * C::X_STAGE, &tmX, bar, kt * C::BK, tt * BT);
+                    last_it = it;
                 }
             }
             if (!ok) {
-                // Let every copy this CTA started land before shared memory goes away.
-                for (int s = 0; s < STAGES; ++s)
-                    if (issued[s]) mbar_wait_drain(full + s, (uint32_t)last_phase[s]);
+                // Let every copy this thread started land before shared memory goes away.
+                for (int j = last_it; j >= 0 && j > last_it - SX; --j)
+                    mbar_wait_drain(xfull + j % SX, (uint32_t)((j / SX) & 1));
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ W producer
+        if (lane == 0) {
+            int it = 0, last_it = -1;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                const int ft = tile % nft;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % SW;
+                    if (!mbar_wait(wempty + s, ((it / SW) & 1) ^ 1, abort_flag, status, 1u)) { ok = false; break; }
+                    mbar_arrive_expect_tx(wfull + s, C::W_STAGE);
+                    tma_load_2d(sW + s * C::W_STAGE, &tmW, wfull + s, kt * C::W_WORDS, ft * C::BF);
+                    last_it = it;
+                }
+            }
+            if (!ok) {
+                for (int j = last_it; j >= 0 && j > last_it - SW; --j)
+                    mbar_wait_drain(wfull + j % SW, (uint32_t)((j / SW) & 1));
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // Per step: wait for X to land and for the A slot to be written, four MMAs,
+        // and a commit each for the X slot and the A slot.
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16_f32(C::BF, BT);
-            int it = 0, tc = 0;
+            int a = 0, xs = 0;          // A slot / X slot of the current step
+            uint32_t aph = 0, xph = 0;  // phase parities of ready[a] and xfull[xs]
+            int tc = 0;
             bool ok = true, any = false;
             for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
                 if (!mbar_wait(dempty, (tc & 1) ^ 1, abort_flag, status, 2u)) { ok = false; break; }
                 tc_fence_after();
-                for (int kt = 0; kt < KT; ++kt, ++it) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(full + s, ph, abort_flag, status, 2u)) { ok = false; break; }
-                    if (!mbar_wait(afull + s, ph, abort_flag, status, 2u)) { ok = false; break; }
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!XRES && !mbar_wait(xfull + xs, xph, abort_flag, status, 2u)) { ok = false; break; }
+                    if (!mbar_wait(ready + a, aph, abort_flag, status, 2u)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(sX + s * C::X_STAGE));
+                    const uint8_t* xt = XRES ? sX + (size_t)kt * C::X_STAGE : sX + xs * C::X_STAGE;
+                    const uint64_t bdesc = smem_desc_sw128(smem_u32(xt));
+                    const uint32_t abase = tmem + C::A_COL + 32u * a;
 #pragma unroll
                     for (int j = 0; j < C::BK / 16; ++j) {
                         // K step of 16 bf16 = 32 bytes inside the swizzled row (+2 in
                         // 16-byte descriptor units); A advances 8 TMEM columns.
-                        tc_mma_ts(tmem + C::D_COL, tmem + C::A_COL + 32u * s + 8u * j,
-                                  bdesc + 2ull * j, idesc, (kt | j) != 0);
+                        tc_mma_ts(tmem + C::D_COL, abase + 8u * j, bdesc + 2ull * j, idesc, (kt | j) != 0);
                     }
+                    if (!XRES) tc_commit(xempty + xs);
+                    tc_commit(done + a);
                     any = true;
-                    tc_commit(done + s);
+                    if (++a == SA) { a = 0; aph ^= 1; }
+                    if (++xs == SX) { xs = 0; xph ^= 1; }
                 }
                 if (!ok) break;
                 tc_commit(dfull);
@@ -175,42 +256,57 @@ __global__ void __launch_bounds__(512, 1)
                 mbar_wait_drain(drain, 0);
             }
         }
-    } else if (warp >= 4 && warp < 12) {
+    } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------------ dequant
-        const int grp_id = (warp - 4) >> 2;                   // takes stages with it % 2 == grp_id
-        const int r = (threadIdx.x - 128) & 127;              // feature row in the tile
+        const int r = threadIdx.x - 128;                      // feature row in the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const int G = K / 64;
+        // The packed tile was written by TMA with a 32-byte (W4) / 64-byte (W8)
+        // swizzle: 16-byte chunk v of row r sits at chunk v ^ sw, which spreads a
+        // quarter-warp's 128-bit reads over all 32 banks.
+        const uint32_t sw = BITS == 4 ? ((r >> 2) & 1) : ((r >> 1) & 3);
         int it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-            const int tt = tile / nft, ft = tile - tt * nft;
-            (void)tt;
+            const int ft = tile % nft;
             const int row = ft * C::BF + r;
             const bool valid = row < N;
             const uint16_t* srow = scales + (int64_t)(valid ? row : 0) * G;
             const uint16_t* brow = biases + (int64_t)(valid ? row : 0) * G;
+            // This group's steps in the tile are kt = kt0, kt0 + 2, ...; the scale and
+            // bias of the next one are loaded while the current one is unpacked.
+            // Loads are unconditional (row 0 stands in for rows past N) and masked
+            // afterwards, so the warp never diverges ahead of its .aligned TMEM ops.
+            // The next step's scale and bias are loaded while this one is unpacked.
+            const uint32_t vmask = valid ? 0xFFFFu : 0u;
+            uint32_t sb_next = (uint32_t)__ldg(srow) & vmask;
+            uint32_t bb_next = (uint32_t)__ldg(brow) & vmask;
             for (int kt = 0; kt < KT; ++kt, ++it) {
-                if ((it & 1) != grp_id) continue;
-                const int s = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1;
-                const uint32_t sb = valid ? (uint32_t)__ldg(srow + kt) : 0u;
-                const uint32_t bb = valid ? (uint32_t)__ldg(brow + kt) : 0u;
-                if (!mbar_wait(full + s, ph, abort_flag, status, 4u)) { ok = false; break; }
-                if (!mbar_wait(done + s, ph ^ 1, abort_flag, status, 4u)) { ok = false; break; }
+                const int ws = it % SW, as = it % SA;
+                const uint32_t sb = sb_next, bb = bb_next;
+                const int kn = kt + 1 < KT ? kt + 1 : kt;
+                sb_next = (uint32_t)__ldg(srow + kn) & vmask;
+                bb_next = (uint32_t)__ldg(brow + kn) & vmask;
+                if (!mbar_wait_warp(wfull + ws, (it / SW) & 1, abort_flag, status, 4u)) { ok = false; break; }
+                constexpr int NV = BITS == 4 ? 2 : 4;         // 16-byte chunks per row
+                uint4 q[NV];
+                const uint8_t* wrow = sW + ws * C::W_STAGE + r * C::W_ROW;
+#pragma unroll
+                for (int v = 0; v < NV; ++v) q[v] = *reinterpret_cast<const uint4*>(wrow + 16 * (v ^ sw));
+                mbar_arrive(wempty + ws);                     // the words are in registers
+                if (!mbar_wait_warp(done + as, ((it / SA) & 1) ^ 1, abort_flag, status, 4u)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t a[32];
-                const uint4* wrow = reinterpret_cast<const uint4*>(sW + s * C::W_STAGE + r * C::W_ROW);
                 if (BITS == 4) {
                     const uint32_t s2 = sb * 0x10001u, b2 = bb * 0x10001u;
 #pragma unroll
-                    for (int v = 0; v < 2; ++v) {
-                        const uint4 q = wrow[v];
-                        const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+                    for (int v = 0; v < NV; ++v) {
+                        const uint32_t wv[4] = {q[v].x, q[v].y, q[v].z, q[v].w};
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t o[4];
-                            dq4_word_natural(wv[w], s2, b2, o);
+                            if (XRES) dq4_word_interleaved(wv[w], s2, b2, o);
+                            else dq4_word_natural(wv[w], s2, b2, o);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) a[4 * (4 * v + w) + j] = o[j];
                         }
@@ -218,9 +314,8 @@ __global__ void __launch_bounds__(512, 1)
                 } else {
                     const float sf = bf16_bits_to_f32(sb), bf = bf16_bits_to_f32(bb);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        const uint4 q = wrow[v];
-                        const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+                    for (int v = 0; v < NV; ++v) {
+                        const uint32_t wv[4] = {q[v].x, q[v].y, q[v].z, q[v].w};
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t o[2];
@@ -230,40 +325,57 @@ __global__ void __launch_bounds__(512, 1)
                         }
                     }
                 }
-                tmem_st32(tmem + lane_base + C::A_COL + 32u * s, a);
+                tmem_st32(tmem + lane_base + C::A_COL + 32u * as, a);
                 tc_wait_st();
                 tc_fence_before();
-                mbar_arrive(afull + s);
+                mbar_arrive(ready + as);
             }
         }
-    } else if (warp >= 12) {
+    } else if (warp >= 8) {
         // ------------------------------------------------------------ epilogue
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         int tc = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
             const int tt = tile / nft, ft = tile - tt * nft;
-            if (!mbar_wait(dfull, tc & 1, abort_flag, status, 8u)) break;
+            if (!mbar_wait_warp(dfull, tc & 1, abort_flag, status, 8u)) break;
             tc_fence_after();
             const int f = ft * C::BF + 32 * (warp & 3) + lane;
             const bool fvalid = f < N;
             const float badd = (bias != nullptr && fvalid) ? bf16_bits_to_f32(bias[f]) : 0.f;
-#pragma unroll 1
-            for (int c = 0; c < BT / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + C::D_COL + 32u * c, v);
+            if (BT == 16) {
+                uint32_t v[16];
+                __syncwarp();
+                tmem_ld16(tmem + lane_base + C::D_COL, v);
                 tc_wait_ld();
-                const int t0 = tt * BT + 32 * c;
                 if (fvalid) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int t = t0 + i;
-                        if (t < M) {
-                            const float val = __uint_as_float(v[i]) + badd;
-                            y[(int64_t)t * N + f] = (uint16_t)(pack_bf16x2(val, 0.f) & 0xFFFFu);
+                    for (int i = 0; i < 16; ++i) {
+                        const int t = tt * BT + i;
+                        if (t < M)
+                            y[(int64_t)t * N + f] =
+                                (uint16_t)(pack_bf16x2(__uint_as_float(v[i]) + badd, 0.f) & 0xFFFFu);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BT / 32; ++c) {
+                    uint32_t v[32];
+                    __syncwarp();
+                    tmem_ld32(tmem + lane_base + C::D_COL + 32u * c, v);
+                    tc_wait_ld();
+                    const int t0 = tt * BT + 32 * c;
+                    if (fvalid) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int t = t0 + i;
+                            if (t < M)
+                                y[(int64_t)t * N + f] =
+                                    (uint16_t)(pack_bf16x2(__uint_as_float(v[i]) + badd, 0.f) & 0xFFFFu);
                         }
                     }
                 }
             }
+            __syncwarp();
             tc_fence_before();
             mbar_arrive(dempty);
         }
@@ -279,6 +391,9 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 // ---------------------------------------------------------------- host side
+// Largest dynamic shared memory a CTA may use on sm_100 (227 KB).
+constexpr size_t kMaxSmem = 232448;
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -292,18 +407,19 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
     return fn;
 }
 
-template <int BITS, int BT, int STAGES>
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const void* bias, void* y, cudaStream_t st,
                         const char** msg) {
-    using C = TcCfg<BITS, BT, STAGES>;
+    using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     auto enc = get_encoder();
     if (!enc) {
         *msg = "cuTensorMapEncodeTiled is unavailable from the driver";
         return cudaErrorNotSupported;
     }
     CUtensorMap tmX, tmW;
-    {
+    std::memset(&tmX, 0, sizeof tmX);
+    if (!XRES) {
         cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
         cuuint64_t strides[1] = {(cuuint64_t)k * 2};
         cuuint32_t box[2] = {(cuuint32_t)C::BK, (cuuint32_t)BT};
@@ -324,28 +440,30 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
         cuuint32_t estr[2] = {1, 1};
         CUresult r = enc(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(wq), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {
             *msg = "cuTensorMapEncodeTiled rejected the packed-weight tensor map";
             return cudaErrorInvalidValue;
         }
     }
+    const size_t smem = smem_bytes<C, XRES, BT>(k);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     static bool configured[64] = {};
-    if (dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, STAGES>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    qmm_tc_kernel<BITS, BT, STAGES><<<grid, 512, C::SMEM_BYTES, st>>>(
-        tmX, tmW, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
-        static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, 384, smem, st>>>(
+        tmX, tmW, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
+        static_cast<const uint16_t*>(biases), static_cast<const uint16_t*>(bias),
+        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
     return cudaGetLastError();
 }
 
@@ -353,11 +471,18 @@ template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                            const void* scales, const void* biases, int64_t n, const void* bias,
                            void* y, cudaStream_t st, const char** msg) {
-    // Tokens per tile: the smallest of 64 / 128 / 256 that covers M, so short
-    // activations do not pay for empty MMA columns.
-    if (m <= 64) return launch_tc_t<BITS, 64, 4>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    if (m <= 128) return launch_tc_t<BITS, 128, 4>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    return launch_tc_t<BITS, 256, 4>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    // Tokens per tile: the smallest of 16 / 64 / 128 / 256 that covers M, so short
+    // activations do not pay for empty MMA columns.  Ring depths fill the shared
+    // memory budget; the packed-weight ring is the deep one.
+    constexpr int SWs = BITS == 4 ? 16 : 12;
+    using CR = TcCfg<BITS, 16, 1, SWs, 14, true>;
+    if (m <= 16 && smem_bytes<CR, true, 16>(k) <= kMaxSmem)
+        return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    if (m <= 16) return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    if (m <= 64) return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    if (m <= 128) return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    constexpr int SX256 = 4;
+    return launch_tc_t<BITS, 256, SX256, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
 }
 
 }  // namespace

@@ -144,10 +144,12 @@ def test_fused_bias(bits, m):
     assert_close(y, want, f"bias m={m} bits={bits}")
 
 
-def test_long_k_small_m_goes_to_the_tensor_core_path():
-    # k above the small-M kernel's shared-memory limit
-    y, want = run_qmm(4, 16384, 128, 4, seed=11)
-    assert_close(y, want, "k=16384 m=4")
+@pytest.mark.parametrize("m,k,bits", [(4, 16384, 4), (8, 12288, 8), (3, 12288, 8), (8, 64, 8),
+                                       (6, 192, 4), (8, 25600, 4)])
+def test_small_m_long_k(m, k, bits):
+    """Long K at small M: staged in shared memory when it fits, else the tensor-core path."""
+    y, want = run_qmm(m, k, 160, bits, seed=11 + m + k)
+    assert_close(y, want, f"m={m} k={k} bits={bits}")
 
 
 @pytest.mark.parametrize("bits,k,n", [(4, 3072, 18432), (8, 12288, 3072)])
