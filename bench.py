@@ -4,7 +4,7 @@
     python bench.py --impl reference ...      # the CPU arm (oracle port of the reference)
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Workloads (data synthetic, seeded):
+Workloads (the benchmark plan's configurations; data synthetic, seeded):
   cfg2  (default) X bf16 [4096, 12288] . W [3072, 12288]^T, W8 g64  -- configs[1]
   cfg1  X [1024, 3072] . W [3072, 3072]^T, W4
   cfg3  X [M<=8, 3072] . W [18432, 3072]^T, W4 (HBM-bound; reports GB/s)
@@ -40,10 +40,10 @@ WORKLOADS = {
     "cfg5": (16384, 3072, 12288, 4, 0.02, "tflops"),
 }
 DESCR = {
-    "cfg1": "BASELINE configs[0]: X bf16[1024,3072] . W[3072,3072]^T, W4 g64",
-    "cfg2": "BASELINE configs[1]: X bf16[4096,12288] . W[3072,12288]^T, W8 g64 (Flux MLP down-proj at 1024^2)",
-    "cfg3": "BASELINE configs[2]: X bf16[8,3072] . W[18432,3072]^T, W4 g64 (adaLN modulation, small-M)",
-    "cfg5": "BASELINE configs[4]: X bf16[16384,3072] . W[12288,3072]^T, W4 g64",
+    "cfg1": "config 1: X bf16[1024,3072] . W[3072,3072]^T, W4 g64",
+    "cfg2": "config 2: X bf16[4096,12288] . W[3072,12288]^T, W8 g64 (Flux MLP down-proj at 1024^2)",
+    "cfg3": "config 3: X bf16[8,3072] . W[18432,3072]^T, W4 g64 (adaLN modulation, small-M)",
+    "cfg5": "config 5: X bf16[16384,3072] . W[12288,3072]^T, W4 g64",
 }
 
 

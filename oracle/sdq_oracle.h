@@ -1,6 +1,6 @@
 /*
  * sdq_oracle.h -- CPU restatement of the affine group-wise quantiser used by
- * andreinknv/stable-diffusion.rs, for TESTS AND THE CPU BASELINE ONLY.
+ * andreinknv/stable-diffusion.rs, for tests and the CPU baseline only.
  *
  * This is test infrastructure.  Only tests/, __graft_entry__.smoke() and the
  * cpu_baseline / reference legs of bench.py may load it, and only as the

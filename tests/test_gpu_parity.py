@@ -4,7 +4,7 @@ Bars (from the task's north star):
   * quantise (packed words, scales, biases) and dequantise: bit-exact;
   * quantised matmul: max|y - ref| / max|ref| <= 1e-2 and cosine >= 0.9999 against the
     f32 (f64-accumulated) dense product of the dequantised weights.
-Full BASELINE sizes are checked through sampled rows/columns and through a
+Full benchmark sizes are checked through sampled rows/columns and through a
 size-independent property: with X = I (M = K) the product is exactly dequant(W)^T.
 """
 from __future__ import annotations
@@ -167,7 +167,7 @@ def test_identity_activation_reproduces_the_dequantised_weight(bits, k, n):
 
 @pytest.mark.parametrize("cfg", ["c1", "c2", "c3", "c5"])
 def test_baseline_configs_sampled(cfg):
-    """BASELINE configs at full size; the oracle checks a sample of rows and columns."""
+    """The benchmark configurations at full size; the oracle checks a sample of rows and columns."""
     shapes = {"c1": (1024, 3072, 3072, 4, 0.02), "c2": (4096, 12288, 3072, 8, 0.01),
               "c3": (8, 3072, 18432, 4, 0.02), "c5": (16384, 3072, 12288, 4, 0.02)}
     m, k, n, bits, sig = shapes[cfg]
