@@ -99,17 +99,14 @@ __global__ void __launch_bounds__(384, 1)
     uint8_t* sW = smem + x_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sW + SW * C::W_STAGE);
     // Step s uses X slot s % SX, W slot s % SW and A slot / barrier pair s % SA.
-    //   xfull[x]   X landed                               count 1 + tx
-    //   xempty[x]  the MMAs that read X slot x finished   count 1 (commit)
     //   wfull[w]   packed W landed                       count 1 + tx
     //   wempty[w]  the dequant group read W slot w        count 128
-    //   ready[a]   A slot written                         count 128
-    //   done[a]    the MMAs that read A slot a finished   count 1 (commit)
-    // The MMA thread itself waits on xfull: the tensor core's shared-memory reads
-    // are ordered after the bulk copy through that wait.
-    uint64_t* xfull = bars;
-    uint64_t* xempty = xfull + SX;
-    uint64_t* wfull = xempty + SX;
+    //   ready[a]   A slot written and X landed: 128 dequant arrivals, plus (with an
+    //              X ring) the X producer's arrive + expect-tx, completed by the
+    //              bulk copy itself -- so the MMA warp observes the copy directly
+    //   done[a]    the MMAs of the step finished          count 1 (one commit per
+    //              step); releases A slot a and the step's X slot
+    uint64_t* wfull = bars;
     uint64_t* wempty = wfull + SW;
     uint64_t* ready = wempty + SW;
     uint64_t* done = ready + SA;
@@ -124,9 +121,8 @@ __global__ void __launch_bounds__(384, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < SX; ++i) { mbar_init(xfull + i, 1); mbar_init(xempty + i, 1); }
         for (int i = 0; i < SW; ++i) { mbar_init(wfull + i, 1); mbar_init(wempty + i, 128); }
-        for (int i = 0; i < SA; ++i) { mbar_init(ready + i, 128); mbar_init(done + i, 1); }
+        for (int i = 0; i < SA; ++i) { mbar_init(ready + i, XRES ? 128 : 129); mbar_init(done + i, 1); }
         mbar_init(dfull, 1);
         mbar_init(dempty, 128);
         mbar_init(drain, 1);
@@ -175,16 +171,19 @@ __global__ void __launch_bounds__(384, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------------ X producer
-        // Step s's X lands on xfull[s % SX]; the slot is reused by step s + SX once the
-        // MMAs of step s are done.
+        // Step s's X completes ready[s % SA]; the slot is reused by step s + SX once
+        // the MMAs of step s are done.
         if (lane == 0 && !XRES) {
             int it = 0, last_it = -1;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 const int tt = tile / nft;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
-                    if (!mbar_wait(xempty + it % SX, ((it / SX) & 1) ^ 1, abort_flag, status, 1u)) { ok = false; break; }
-                    uint64_t* bar = xfull + it % SX;
+                    if (it >= SX) {
+                        const int prev = it - SX;       // the step that last used this slot
+                        if (!mbar_wait(done + prev % SA, (prev / SA) & 1, abort_flag, status, 1u)) { ok = false; break; }
+                    }
+                    uint64_t* bar = ready + it % SA;
                     mbar_arrive_expect_tx(bar, C::X_STAGE);
                     tma_load_2d(sX + (it % SX) * C::X_STAGE, &tmX, bar, kt * C::BK, tt * BT);
                     last_it = it;
@@ -193,7 +192,7 @@ __global__ void __launch_bounds__(384, 1)
             if (!ok) {
                 // Let every copy this thread started land before shared memory goes away.
                 for (int j = last_it; j >= 0 && j > last_it - SX; --j)
-                    mbar_wait_drain(xfull + j % SX, (uint32_t)((j / SX) & 1));
+                    mbar_wait_drain(ready + j % SA, (uint32_t)((j / SA) & 1));
             }
         }
     } else if (warp == 2) {
@@ -218,43 +217,41 @@ __global__ void __launch_bounds__(384, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        // Per step: wait for X to land and for the A slot to be written, four MMAs,
-        // and a commit each for the X slot and the A slot.
-        if (lane == 0) {
-            const uint32_t idesc = idesc_bf16_f32(C::BF, BT);
-            int a = 0, xs = 0;          // A slot / X slot of the current step
-            uint32_t aph = 0, xph = 0;  // phase parities of ready[a] and xfull[xs]
-            int tc = 0;
-            bool ok = true, any = false;
-            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
-                if (!mbar_wait(dempty, (tc & 1) ^ 1, abort_flag, status, 2u)) { ok = false; break; }
+        // The whole warp runs the loop converged, so descriptors and TMEM addresses
+        // are warp-uniform; one elected lane issues the MMAs and the commits.  Per
+        // step: one wait (A written, X landed), four MMAs, one commit.
+        const uint32_t idesc = idesc_bf16_f32(C::BF, BT);
+        int a = 0, xs = 0;              // A slot / X slot of the current step
+        uint32_t aph = 0;               // phase parity of ready[a] / done[a]
+        int tc = 0;
+        bool ok = true, any = false;
+        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
+            if (!mbar_wait_warp(dempty, (tc & 1) ^ 1, abort_flag, status, 2u)) { ok = false; break; }
+            tc_fence_after();
+            for (int kt = 0; kt < KT; ++kt) {
+                if (!mbar_wait_warp(ready + a, aph, abort_flag, status, 2u)) { ok = false; break; }
                 tc_fence_after();
-                for (int kt = 0; kt < KT; ++kt) {
-                    if (!XRES && !mbar_wait(xfull + xs, xph, abort_flag, status, 2u)) { ok = false; break; }
-                    if (!mbar_wait(ready + a, aph, abort_flag, status, 2u)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint8_t* xt = XRES ? sX + (size_t)kt * C::X_STAGE : sX + xs * C::X_STAGE;
-                    const uint64_t bdesc = smem_desc_sw128(smem_u32(xt));
-                    const uint32_t abase = tmem + C::A_COL + 32u * a;
+                const uint8_t* xt = XRES ? sX + (size_t)kt * C::X_STAGE : sX + xs * C::X_STAGE;
+                const uint64_t bdesc = smem_desc_sw128(smem_u32(xt));
+                const uint32_t abase = tmem + C::A_COL + 32u * a;
 #pragma unroll
-                    for (int j = 0; j < C::BK / 16; ++j) {
-                        // K step of 16 bf16 = 32 bytes inside the swizzled row (+2 in
-                        // 16-byte descriptor units); A advances 8 TMEM columns.
-                        tc_mma_ts(tmem + C::D_COL, abase + 8u * j, bdesc + 2ull * j, idesc, (kt | j) != 0);
-                    }
-                    if (!XRES) tc_commit(xempty + xs);
-                    tc_commit(done + a);
-                    any = true;
-                    if (++a == SA) { a = 0; aph ^= 1; }
-                    if (++xs == SX) { xs = 0; xph ^= 1; }
+                for (int j = 0; j < C::BK / 16; ++j) {
+                    // K step of 16 bf16 = 32 bytes inside the swizzled row (+2 in
+                    // 16-byte descriptor units); A advances 8 TMEM columns.
+                    tc_mma_ts_elect(tmem + C::D_COL, abase + 8u * j, bdesc + 2ull * j, idesc,
+                                    (kt | j) != 0);
                 }
-                if (!ok) break;
-                tc_commit(dfull);
+                tc_commit_elect(done + a);
+                any = true;
+                if (++a == SA) { a = 0; aph ^= 1; }
+                if (++xs == SX) xs = 0;
             }
-            if (!ok && any) {
-                tc_commit(drain);
-                mbar_wait_drain(drain, 0);
-            }
+            if (!ok) break;
+            tc_commit_elect(dfull);
+        }
+        if (!ok && any) {
+            tc_commit_elect(drain);
+            mbar_wait_drain(drain, 0);
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------------ dequant
