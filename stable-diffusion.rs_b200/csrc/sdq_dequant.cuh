@@ -72,18 +72,37 @@ __device__ __forceinline__ void dq4_word_interleaved(uint32_t w, uint32_t s2, ui
 
 // ---- W8: one packed word (bytes q0..q3, q0 least significant) --------------
 // Natural order: out[0] = (q0, q1), out[1] = (q2, q3).  q does not fit a bf16
-// magic-number mantissa, so it is widened through binary32 (2^23 + q) - 2^23.
+// magic-number mantissa, so it is widened through binary32, two lanes at a
+// time with the packed f32x2 instructions: (2^23 + q) - 2^23 is exact, then
+// one fma per value rounds the exact s*q + b to binary32, and the final
+// conversion rounds it once more to bf16 (innocuous: 24 >= 2*8 + 2 bits).
+__device__ __forceinline__ uint64_t f32x2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f32x2_dup(float v) {
+    const uint64_t u = __float_as_uint(v);
+    return u | (u << 32);
+}
 __device__ __forceinline__ void dq8_word_natural(uint32_t w, float s, float b,
                                                  uint32_t (&out)[2]) {
-    float f[4];
+    constexpr uint64_t kMagic2 = 0x4B0000004B000000ull;   // (2^23, 2^23)
+    const uint64_t s2 = f32x2_dup(s), b2 = f32x2_dup(b);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        // byte0 <- w.byte j, bytes 1,2 <- 0x00, byte3 <- 0x4B  => 2^23 + q
-        const uint32_t bits = prmt(w, 0x4B000000u, (uint32_t)j | 0x7440u);
-        f[j] = fmaf(s, __uint_as_float(bits) - 8388608.0f, b);
+    for (int h = 0; h < 2; ++h) {
+        // byte0 <- w.byte(2h / 2h+1), bytes 1,2 <- 0x00, byte3 <- 0x4B  => 2^23 + q
+        const uint32_t lo = prmt(w, 0x4B000000u, (uint32_t)(2 * h) | 0x7440u);
+        const uint32_t hi = prmt(w, 0x4B000000u, (uint32_t)(2 * h + 1) | 0x7440u);
+        const uint64_t q2 = f32x2_sub((uint64_t)lo | ((uint64_t)hi << 32), kMagic2);
+        const uint64_t r = f32x2_fma(s2, q2, b2);
+        out[h] = pack_bf16x2(__uint_as_float((uint32_t)r), __uint_as_float((uint32_t)(r >> 32)));
     }
-    out[0] = pack_bf16x2(f[0], f[1]);
-    out[1] = pack_bf16x2(f[2], f[3]);
 }
 
 }  // namespace sdq

@@ -23,12 +23,14 @@
 //   A ring  (SA slots in TMEM)  dequant      -> MMA
 // so the weight stream and its unpacking run many steps ahead of the MMAs.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of the X ring (idle when X is resident)
 //   warp 1      TMEM allocator and MMA issuer
 //   warp 2      TMA producer of the W ring
 //   warps 4-7   dequant warpgroup; thread r owns feature row r of the tile
-//   warps 8-11  epilogue: TMEM -> registers -> (+bias) -> bf16 -> global
+//   warps 8-15  epilogue, two warpgroups taking alternate 32-token chunks of
+//               the accumulator: TMEM -> registers (+bias, packed to bf16),
+//               release the accumulator, then store to global
 // Exactly one warp stores to each TMEM sub-partition (lanes 32w..32w+31).  With
 // two dequant warpgroups taking alternate steps -- two warps of one SM
 // sub-partition storing different columns of the same TMEM lanes at the same
@@ -67,7 +69,8 @@ struct TcCfg {
     static constexpr uint32_t D_COL = 0;                   // accumulator columns [0, BT)
     static constexpr uint32_t A_COL = BT < 32 ? 32 : BT;   // A slots: 32 columns each
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int RING_BYTES = (XRES ? 0 : SX * X_STAGE) + SW * W_STAGE;
+    static constexpr int Y_STAGE = BT * BF * 2;            // bf16 staging of one output tile
+    static constexpr int RING_BYTES = (XRES ? 0 : SX * X_STAGE) + SW * W_STAGE + Y_STAGE;
     static_assert(BT % 16 == 0 && BT >= 16 && BT <= 256, "MMA N must be 16..256, step 16");
     static_assert(A_COL + 32 * SA <= TMEM_COLS, "A slots must fit beside the accumulator");
     static_assert(!XRES || BT == 16, "resident activations only for the 16-token tile");
@@ -83,11 +86,12 @@ size_t smem_bytes(int64_t k) {
 }
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                  const __grid_constant__ CUtensorMap tmY,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
                   const uint16_t* __restrict__ biases, const uint16_t* __restrict__ bias,
-                  uint16_t* __restrict__ y, int M, int N, int K) {
+                  uint16_t* __restrict__ y, int M, int N, int K, int y_tma) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -97,7 +101,8 @@ __global__ void __launch_bounds__(384, 1)
     uint8_t* sX = smem;
     const size_t x_bytes = XRES ? (size_t)KT * C::X_STAGE : (size_t)SX * C::X_STAGE;
     uint8_t* sW = smem + x_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sW + SW * C::W_STAGE);
+    uint8_t* sY = sW + SW * C::W_STAGE;                   // [BT tokens][128 features] bf16
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sY + C::Y_STAGE);
     // Step s uses X slot s % SX, W slot s % SW and A slot / barrier pair s % SA.
     //   wfull[w]   packed W landed                       count 1 + tx
     //   wempty[w]  the dequant group read W slot w        count 128
@@ -111,7 +116,7 @@ __global__ void __launch_bounds__(384, 1)
     uint64_t* ready = wempty + SW;
     uint64_t* done = ready + SA;
     uint64_t* dfull = done + SA;             // accumulator complete       count 1 (commit)
-    uint64_t* dempty = dfull + 1;            // accumulator drained        count 128
+    uint64_t* dempty = dfull + 1;            // accumulator drained        count 256
     uint64_t* drain = dfull + 2;             // abort drain of the MMA pipe
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -124,12 +129,13 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < SW; ++i) { mbar_init(wfull + i, 1); mbar_init(wempty + i, 128); }
         for (int i = 0; i < SA; ++i) { mbar_init(ready + i, XRES ? 128 : 129); mbar_init(done + i, 1); }
         mbar_init(dfull, 1);
-        mbar_init(dempty, 128);
+        mbar_init(dempty, 256);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
         if (!XRES) tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
+        if (y_tma) tma_prefetch_desc(&tmY);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -168,6 +174,7 @@ __global__ void __launch_bounds__(384, 1)
     const int nft = (N + C::BF - 1) / C::BF;
     const int ntt = (M + BT - 1) / BT;
     const int ntiles = nft * ntt;
+
 
     if (warp == 0) {
         // ------------------------------------------------------------ X producer
@@ -330,52 +337,71 @@ __global__ void __launch_bounds__(384, 1)
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------ epilogue
+        // Group e takes chunks e, e + 2, ... (32 tokens; one 16-token chunk when
+        // BT = 16): TMEM -> registers (+bias) -> bf16 into the shared staging tile
+        // [token][feature].  The accumulator is released as soon as both groups
+        // have read it.  Then one thread per group writes each chunk with a TMA
+        // tensor store, which clips tokens >= M and features >= N; when Y's row
+        // pitch or base is not 16-byte aligned the group copies the chunk with
+        // plain stores instead.  A timed-out wait is made group-uniform by the
+        // reducing barrier, so no warp of the group is left at a named barrier.
+        constexpr int CW = BT < 32 ? BT : 32;             // tokens per chunk
+        constexpr int NCH = BT / CW;                      // chunks per tile
+        const int e = (warp - 8) >> 2;
+        const int fl = 32 * (warp & 3) + lane;            // feature row within the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const bool leader = (warp & 3) == 0 && lane == 0;
         int tc = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
             const int tt = tile / nft, ft = tile - tt * nft;
-            if (!mbar_wait_warp(dfull, tc & 1, abort_flag, status, 8u)) break;
-            tc_fence_after();
-            const int f = ft * C::BF + 32 * (warp & 3) + lane;
-            const bool fvalid = f < N;
-            const float badd = (bias != nullptr && fvalid) ? bf16_bits_to_f32(bias[f]) : 0.f;
-            if (BT == 16) {
-                uint32_t v[16];
-                __syncwarp();
-                tmem_ld16(tmem + lane_base + C::D_COL, v);
-                tc_wait_ld();
-                if (fvalid) {
+            const int f = ft * C::BF + fl;
+            const float badd = (bias != nullptr && f < N) ? bf16_bits_to_f32(bias[f]) : 0.f;
+            // The staging chunks of this group must have been read by the previous
+            // tile's stores before they are overwritten.
+            if (leader && y_tma) bulk_wait_group_read0();
+            named_barrier_sync(1 + e, 128);
+            const bool ok = mbar_wait_warp(dfull, tc & 1, abort_flag, status, 8u);
+            if (ok) {
+                tc_fence_after();
+                for (int c = e; c < NCH; c += 2) {
+                    uint16_t* yrow = reinterpret_cast<uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int t = tt * BT + i;
-                        if (t < M)
-                            y[(int64_t)t * N + f] =
-                                (uint16_t)(pack_bf16x2(__uint_as_float(v[i]) + badd, 0.f) & 0xFFFFu);
+                    for (int h = 0; h < CW / 16; ++h) {
+                        uint32_t v[16];
+                        __syncwarp();
+                        tmem_ld16(tmem + lane_base + C::D_COL + (uint32_t)(CW * c + 16 * h), v);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            yrow[(16 * h + j) * C::BF] =
+                                (uint16_t)(pack_bf16x2(__uint_as_float(v[j]) + badd, 0.f) & 0xFFFFu);
                     }
                 }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < BT / 32; ++c) {
-                    uint32_t v[32];
-                    __syncwarp();
-                    tmem_ld32(tmem + lane_base + C::D_COL + 32u * c, v);
-                    tc_wait_ld();
-                    const int t0 = tt * BT + 32 * c;
-                    if (fvalid) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int t = t0 + i;
-                            if (t < M)
-                                y[(int64_t)t * N + f] =
-                                    (uint16_t)(pack_bf16x2(__uint_as_float(v[i]) + badd, 0.f) & 0xFFFFu);
-                        }
-                    }
+                __syncwarp();
+                tc_fence_before();
+                mbar_arrive(dempty);
+                if (y_tma) fence_proxy_async_smem();
+            }
+            if (!named_barrier_and(1 + e, 128, ok)) break;
+            if (y_tma) {
+                if (leader) {
+                    for (int c = e; c < NCH; c += 2)
+                        if (tt * BT + c * CW < M)
+                            tma_store_2d(&tmY, sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
+                                         tt * BT + c * CW);
+                    bulk_commit_group();
+                }
+            } else if (f < N) {
+                for (int c = e; c < NCH; c += 2) {
+                    const uint16_t* yrow =
+                        reinterpret_cast<const uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
+                    const int t0 = tt * BT + c * CW;
+                    const int nr = M - t0 < CW ? M - t0 : CW;
+                    for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * N + f] = yrow[r * C::BF];
                 }
             }
-            __syncwarp();
-            tc_fence_before();
-            mbar_arrive(dempty);
         }
+        if (leader && y_tma) bulk_wait_group0();
     }
 
     tc_fence_before();
@@ -444,6 +470,24 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
             return cudaErrorInvalidValue;
         }
     }
+    // Y is written by TMA tensor stores when its row pitch and base are 16-byte
+    // aligned; otherwise the tensor map stays unused and the epilogue stores.
+    CUtensorMap tmY;
+    std::memset(&tmY, 0, sizeof(tmY));
+    const bool y_tma = (n % 8) == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+    if (y_tma) {
+        cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+        cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+        cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)(BT < 32 ? BT : 32)};
+        cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&tmY, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            *msg = "cuTensorMapEncodeTiled rejected the output tensor map";
+            return cudaErrorInvalidValue;
+        }
+    }
     const size_t smem = smem_bytes<C, XRES, BT>(k);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -457,10 +501,10 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     }
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, 384, smem, st>>>(
-        tmX, tmW, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, 512, smem, st>>>(
+        tmX, tmW, tmY, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), static_cast<const uint16_t*>(bias),
-        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
+        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k, y_tma ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -478,8 +522,8 @@ cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* 
     if (m <= 16) return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
     if (m <= 64) return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
     if (m <= 128) return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    constexpr int SX256 = 4;
-    return launch_tc_t<BITS, 256, SX256, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    constexpr int SW256 = BITS == 4 ? 8 : 4;
+    return launch_tc_t<BITS, 256, 4, SW256, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
 }
 
 }  // namespace

@@ -138,6 +138,15 @@ def test_large_m(bits, m, k, n):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m", [3, 130, 300])
+@pytest.mark.parametrize("n", [1, 37, 203])
+def test_output_width_not_a_multiple_of_8(bits, m, n):
+    """Rows of Y that are not 16-byte multiples are written with plain stores, not TMA."""
+    y, want = run_qmm(m, 192, n, bits, seed=17 + m + n, with_bias=True)
+    assert_close(y, want, f"odd n={n} m={m} bits={bits}")
+
+
+@pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("m", [4, 300])
 def test_fused_bias(bits, m):
     y, want = run_qmm(m, 256, 192, bits, seed=5 + m, with_bias=True)
