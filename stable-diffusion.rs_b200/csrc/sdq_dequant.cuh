@@ -45,7 +45,7 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h16) {
 constexpr uint32_t kBf16x2_128 = 0x43004300u;  // (128.0, 128.0)
 
 // ---- W4: one packed word (nibbles n0..n7, n0 least significant) -----------
-// Natural order: out[j] = (lo: k=2j, hi: k=2j+1) as bf16x2 of s*q + b.
+// out[j] = (lo: k=2j, hi: k=2j+1) as bf16x2 of s*q + b.
 __device__ __forceinline__ void dq4_word_natural(uint32_t w, uint32_t s2, uint32_t b2,
                                                  uint32_t (&out)[4]) {
     const uint32_t lo = w & 0x0F0F0F0Fu;          // bytes n0 n2 n4 n6
@@ -56,16 +56,6 @@ __device__ __forceinline__ void dq4_word_natural(uint32_t w, uint32_t s2, uint32
         const uint32_t sel = (uint32_t)j | ((uint32_t)j << 4) | ((uint32_t)(4 + j) << 8) |
                              ((uint32_t)(4 + j) << 12);
         const uint32_t t = (prmt(lo, hi, sel) & 0x00FF00FFu) | kBf16x2_128;  // 128 + q
-        out[j] = bf16x2_fma(bf16x2_sub(t, kBf16x2_128), s2, b2);
-    }
-}
-// Interleaved order: out[j] = (lo: k=j, hi: k=j+4).  Cheaper (no byte
-// permute); used where the activation operand is staged in the same order.
-__device__ __forceinline__ void dq4_word_interleaved(uint32_t w, uint32_t s2, uint32_t b2,
-                                                     uint32_t (&out)[4]) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t t = ((w >> (4 * j)) & 0x000F000Fu) | kBf16x2_128;
         out[j] = bf16x2_fma(bf16x2_sub(t, kBf16x2_128), s2, b2);
     }
 }

@@ -79,6 +79,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// mbar_wait for roles off the critical path (producers running ahead, the
+// epilogue waiting out a whole tile): after the first failed test the thread
+// sleeps `sleep_ns` between tests, so its spinning does not take issue slots
+// from the dequant warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                unsigned int* status, unsigned int status_bit,
+                                                unsigned int sleep_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(sleep_ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15u) == 0u) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                atomicOr(status, status_bit);
+                return false;
+            }
+        }
+    }
+}
+
 // Warp-collective form of mbar_wait for warps that go on to issue
 // .sync.aligned tcgen05 instructions (tcgen05.st / ld / wait::*): each lane
 // waits (and so acquires) on its own, then the warp votes, which also

@@ -10,7 +10,8 @@
 //     passes through shared memory;
 //   * B = the activation tile, BT tokens x 64 k bf16 in shared memory with
 //     128-byte swizzle (loaded per step by TMA, or -- for BT = 16 when X fits
-//     -- staged once at kernel start and kept resident);
+//     -- loaded whole by TMA at kernel start and kept resident; rows >= M
+//     arrive as zeros from the copy's out-of-range fill);
 //   * D = 128 x BT f32 accumulator in TMEM (tcgen05.mma kind::f16, issued by
 //     one thread).
 // With tokens on the MMA N side, every dequantised weight element feeds BT
@@ -24,7 +25,7 @@
 // so the weight stream and its unpacking run many steps ahead of the MMAs.
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer of the X ring (idle when X is resident)
+//   warp 0      TMA producer of the X ring (or of the resident X)
 //   warp 1      TMEM allocator and MMA issuer
 //   warp 2      TMA producer of the W ring
 //   warps 4-7   dequant warpgroup; thread r owns feature row r of the tile
@@ -118,7 +119,8 @@ __global__ void __launch_bounds__(512, 1)
     uint64_t* dfull = done + SA;             // accumulator complete       count 1 (commit)
     uint64_t* dempty = dfull + 1;            // accumulator drained        count 256
     uint64_t* drain = dfull + 2;             // abort drain of the MMA pipe
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* xfull = dfull + 3;             // resident X landed          count 1 + tx
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     unsigned int* status = &g_tc_status;
 
@@ -131,40 +133,16 @@ __global__ void __launch_bounds__(512, 1)
         mbar_init(dfull, 1);
         mbar_init(dempty, 256);
         mbar_init(drain, 1);
+        mbar_init(xfull, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        if (!XRES) tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
         if (y_tma) tma_prefetch_desc(&tmY);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
-    }
-    if (XRES) {
-        // Stage all of X (16 rows, zero beyond M) once, in the 128B-swizzled K-major
-        // layout the MMA reads, with k permuted inside each 8-element run to
-        // (0,4,1,5,2,6,3,7) -- the order in which the dequant's nibble unpack emits
-        // weight pairs (see dq4_word_interleaved).  8-bit weights unpack in natural
-        // order, so their activations stay natural.
-        const int chunks = KT * 16 * 8;
-        for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
-            const int c = i & 7, row = (i >> 3) & 15, kt = i >> 7;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (row < M) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(xg + (int64_t)row * K + kt * 64 + c * 8);
-                if (BITS == 4) {
-                    v.x = prmt(raw.x, raw.z, 0x5410u);
-                    v.y = prmt(raw.x, raw.z, 0x7632u);
-                    v.z = prmt(raw.y, raw.w, 0x5410u);
-                    v.w = prmt(raw.y, raw.w, 0x7632u);
-                } else {
-                    v = raw;
-                }
-            }
-            *reinterpret_cast<uint4*>(sX + (size_t)kt * C::X_STAGE + row * 128 + ((c ^ (row & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();
     }
     tc_fence_before();
     __syncthreads();
@@ -180,7 +158,15 @@ __global__ void __launch_bounds__(512, 1)
         // ------------------------------------------------------------ X producer
         // Step s's X completes ready[s % SA]; the slot is reused by step s + SX once
         // the MMAs of step s are done.
-        if (lane == 0 && !XRES) {
+        if (lane == 0 && XRES) {
+            // All KT tiles of X (16 rows; rows >= M zero-filled) on one barrier.
+            mbar_arrive_expect_tx(xfull, (uint32_t)KT * C::X_STAGE);
+            for (int kt = 0; kt < KT; ++kt)
+                tma_load_2d(sX + (size_t)kt * C::X_STAGE, &tmX, xfull, kt * C::BK, 0);
+            // The copies must land before shared memory is released, whatever the
+            // other roles do.
+            mbar_wait_drain(xfull, 0);
+        } else if (lane == 0) {
             int it = 0, last_it = -1;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -188,7 +174,7 @@ __global__ void __launch_bounds__(512, 1)
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     if (it >= SX) {
                         const int prev = it - SX;       // the step that last used this slot
-                        if (!mbar_wait(done + prev % SA, (prev / SA) & 1, abort_flag, status, 1u)) { ok = false; break; }
+                        if (!mbar_wait_sleep(done + prev % SA, (prev / SA) & 1, abort_flag, status, 1u, 32)) { ok = false; break; }
                     }
                     uint64_t* bar = ready + it % SA;
                     mbar_arrive_expect_tx(bar, C::X_STAGE);
@@ -211,7 +197,7 @@ __global__ void __launch_bounds__(512, 1)
                 const int ft = tile % nft;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % SW;
-                    if (!mbar_wait(wempty + s, ((it / SW) & 1) ^ 1, abort_flag, status, 1u)) { ok = false; break; }
+                    if (!mbar_wait_sleep(wempty + s, ((it / SW) & 1) ^ 1, abort_flag, status, 1u, 32)) { ok = false; break; }
                     mbar_arrive_expect_tx(wfull + s, C::W_STAGE);
                     tma_load_2d(sW + s * C::W_STAGE, &tmW, wfull + s, kt * C::W_WORDS, ft * C::BF);
                     last_it = it;
@@ -231,7 +217,7 @@ __global__ void __launch_bounds__(512, 1)
         int a = 0, xs = 0;              // A slot / X slot of the current step
         uint32_t aph = 0;               // phase parity of ready[a] / done[a]
         int tc = 0;
-        bool ok = true, any = false;
+        bool ok = !XRES || mbar_wait_warp(xfull, 0, abort_flag, status, 2u), any = false;
         for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tc) {
             if (!mbar_wait_warp(dempty, (tc & 1) ^ 1, abort_flag, status, 2u)) { ok = false; break; }
             tc_fence_after();
@@ -277,8 +263,6 @@ __global__ void __launch_bounds__(512, 1)
             const bool valid = row < N;
             const uint16_t* srow = scales + (int64_t)(valid ? row : 0) * G;
             const uint16_t* brow = biases + (int64_t)(valid ? row : 0) * G;
-            // This group's steps in the tile are kt = kt0, kt0 + 2, ...; the scale and
-            // bias of the next one are loaded while the current one is unpacked.
             // Loads are unconditional (row 0 stands in for rows past N) and masked
             // afterwards, so the warp never diverges ahead of its .aligned TMEM ops.
             // The next step's scale and bias are loaded while this one is unpacked.
@@ -309,8 +293,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
                             uint32_t o[4];
-                            if (XRES) dq4_word_interleaved(wv[w], s2, b2, o);
-                            else dq4_word_natural(wv[w], s2, b2, o);
+                            dq4_word_natural(wv[w], s2, b2, o);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) a[4 * (4 * v + w) + j] = o[j];
                         }
@@ -360,7 +343,8 @@ __global__ void __launch_bounds__(512, 1)
             // tile's stores before they are overwritten.
             if (leader && y_tma) bulk_wait_group_read0();
             named_barrier_sync(1 + e, 128);
-            const bool ok = mbar_wait_warp(dfull, tc & 1, abort_flag, status, 8u);
+            const bool ok = __all_sync(0xffffffffu,
+                                       mbar_wait_sleep(dfull, tc & 1, abort_flag, status, 8u, 64));
             if (ok) {
                 tc_fence_after();
                 for (int c = e; c < NCH; c += 2) {
@@ -441,8 +425,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
         return cudaErrorNotSupported;
     }
     CUtensorMap tmX, tmW;
-    std::memset(&tmX, 0, sizeof tmX);
-    if (!XRES) {
+    {
         cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
         cuuint64_t strides[1] = {(cuuint64_t)k * 2};
         cuuint32_t box[2] = {(cuuint32_t)C::BK, (cuuint32_t)BT};
