@@ -200,8 +200,12 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
         return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
     if ((rc = check_device())) return rc;
     const char* msg = nullptr;
-    const cudaError_t e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y,
-                                        static_cast<cudaStream_t>(stream), &msg);
+    bool taken = false;
+    cudaError_t e = launch_qmv(x, m, k, wq, scales, biases, n, bits, bias, y,
+                               static_cast<cudaStream_t>(stream), &msg, &taken);
+    if (e == cudaSuccess && !taken)
+        e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y,
+                          static_cast<cudaStream_t>(stream), &msg);
     if (e != cudaSuccess) {
         if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
         return cuda_fail("sdq_quantized_matmul: tensor-core kernel", e);
@@ -212,14 +216,16 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
 int sdq_device_status(void* stream) {
     int rc;
     if ((rc = check_device())) return rc;
-    unsigned int st = 0;
+    unsigned int st = 0, sv = 0;
     cudaError_t e = read_and_clear_status(&st, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = read_and_clear_qmv_status(&sv, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("sdq_device_status", e);
-    if (st != 0) {
+    if (st != 0 || sv != 0) {
         return fail(SDQ_ERR_TIMEOUT,
-                    "a device-side wait gave up (status bits 0x%x: 1 producer, 2 MMA, 4 dequant, "
-                    "8 epilogue); the kernel returned early and its output is incomplete",
-                    st);
+                    "a device-side wait gave up (tensor-core kernel bits 0x%x: 1 producer, 2 MMA, "
+                    "4 dequant, 8 epilogue; small-M kernel bits 0x%x: 1 producer, 2 activations, "
+                    "4 weights); the kernel returned early and its output is incomplete",
+                    st, sv);
     }
     return ok();
 }

@@ -1,13 +1,22 @@
 // sdq_internal.h -- declarations shared between the kernel files and the C ABI.
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 namespace sdq {
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
+
+// cuTensorMapEncodeTiled from the driver (nullptr when unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// Opt-in dynamic shared memory per block on sm_100 (227 KB).
+constexpr size_t kQmvMaxSmem = 232448;
 
 cudaError_t launch_quantize(const void* w, bool w_bf16, int64_t n, int64_t k, int bits,
                             uint32_t* wq, void* scales, void* biases, cudaStream_t st);
@@ -21,7 +30,15 @@ cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* w
                           const void* scales, const void* biases, int64_t n, int bits,
                           const void* bias, void* y, cudaStream_t st, const char** msg);
 
-// Device status word (see sdq_ptx.cuh).
+// Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs).
+// Sets *taken = false, launching nothing, for shapes it does not serve (M > 8, or X too
+// large to stay resident beside the weight ring); the caller then uses launch_qmm_tc.
+cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
+                       const void* biases, int64_t n, int bits, const void* bias, void* y,
+                       cudaStream_t st, const char** msg, bool* taken);
+
+// Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st);
+cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st);
 
 }  // namespace sdq

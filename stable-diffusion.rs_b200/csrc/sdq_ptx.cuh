@@ -59,6 +59,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete may be
+// suspended (issuing nothing) until the phase completes or `hint_ns` passes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the phase with `parity` to complete, giving up after kWaitLimitNs or
 // as soon as another role of this CTA has raised `*abort`.  Returns false when
 // it gave up (and then sets the abort flag and the global status bit).
@@ -115,6 +129,29 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
     return __all_sync(0xffffffffu, ok);
 }
 
+// mbar_wait_warp whose tests suspend the waiting warp for up to `hint_ns` instead of
+// spinning, for consumers that share their sub-partition with other busy warps.
+__device__ __forceinline__ bool mbar_wait_warp_parked(uint64_t* bar, uint32_t parity,
+                                                      volatile int* abort, unsigned int* status,
+                                                      unsigned int status_bit, uint32_t hint_ns) {
+    bool ok = mbar_try_wait_hint(bar, parity, hint_ns);
+    if (!ok) {
+        const unsigned long long t0 = globaltimer();
+        for (uint32_t it = 1;; ++it) {
+            if (mbar_try_wait_hint(bar, parity, hint_ns)) { ok = true; break; }
+            if ((it & 7u) == 0u) {
+                if (*abort) break;
+                if (globaltimer() - t0 > kWaitLimitNs) {
+                    *abort = 1;
+                    atomicOr(status, status_bit);
+                    break;
+                }
+            }
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait used only while draining after an abort: ignores the abort flag.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
     const unsigned long long t0 = globaltimer();
@@ -137,6 +174,34 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+// 1-D bulk copy global -> shared of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned), completion counted on `bar` in bytes.  No multicast.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+// Ampere-style asynchronous copy of 4 or 8 bytes global -> shared; `src_bytes` = 0
+// writes zeros instead of reading.  cp_async_arrive makes `bar` receive one
+// arrival once all of this thread's earlier cp.async copies have landed (the
+// barrier's expected count must include it).
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void* smem_dst, const void* src, uint32_t src_bytes) {
+    static_assert(BYTES == 4 || BYTES == 8, "cp.async.ca copies 4, 8 or 16 bytes");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "n"(BYTES), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 // L2 eviction-priority policies for the cache_hint operand.
 __device__ __forceinline__ uint64_t policy_evict_first() {

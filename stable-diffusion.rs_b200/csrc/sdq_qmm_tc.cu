@@ -399,27 +399,15 @@ __global__ void __launch_bounds__(512, 1)
 
 // ---------------------------------------------------------------- host side
 // Largest dynamic shared memory a CTA may use on sm_100 (227 KB).
-constexpr size_t kMaxSmem = 232448;
+constexpr size_t kMaxSmem = kQmvMaxSmem;
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const void* bias, void* y, cudaStream_t st,
                         const char** msg) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
-    auto enc = get_encoder();
+    auto enc = tensor_map_encoder();
     if (!enc) {
         *msg = "cuTensorMapEncodeTiled is unavailable from the driver";
         return cudaErrorNotSupported;
@@ -510,6 +498,19 @@ cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* 
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
 
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,

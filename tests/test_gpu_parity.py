@@ -138,6 +138,18 @@ def test_large_m(bits, m, k, n):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("k,n", [(256, 1), (256, 37), (512, 203), (3072, 2048), (3072, 4096),
+                                 (3072, 9216), (1024, 18432)])
+def test_small_m_weight_stream(bits, m, k, n):
+    """M <= 8 with K a whole number of 128-byte weight rows: the streaming kernel, at each of its
+    tile heights (N = 2048 / 4096 / 9216 / 18432 pick 16 / 32 / 64 / 128 rows) and ragged N."""
+    y, want = run_qmm(m, k, n, bits, seed=31 * m + k + n, with_bias=(n % 2 == 1))
+    assert y.shape == (m, n)
+    assert_close(y, want, f"stream m={m} k={k} n={n} bits={bits}")
+
+
+@pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("m", [3, 130, 300])
 @pytest.mark.parametrize("n", [1, 37, 203])
 def test_output_width_not_a_multiple_of_8(bits, m, n):
