@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace sdq {
@@ -162,12 +163,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 // ---------------------------------------------------------------- TMA
-__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 // 2-D tiled load global -> shared, completion counted on `bar` in bytes.
 // No multicast: every CTA loads its own tiles.
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tmap, uint64_t* bar,
                                             int32_t c0, int32_t c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -259,6 +260,17 @@ __device__ __forceinline__ void tc_mma_ts_elect(uint32_t d_tmem, uint32_t a_tmem
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// SS form: A and B both from shared memory through descriptors; one elected lane issues.
+__device__ __forceinline__ void tc_mma_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 __device__ __forceinline__ void tc_commit_elect(uint64_t* bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
@@ -283,7 +295,7 @@ __device__ __forceinline__ void tc_wait_ld() {
 
 // 2-D tiled store shared -> global (bulk async group); out-of-range rows and
 // columns of the box are not written.
-__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t c0,
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tmap, const void* smem_src, int32_t c0,
                                              int32_t c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -298,6 +310,10 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// ... all but the most recent one.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_group0() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -305,6 +321,24 @@ __device__ __forceinline__ void bulk_wait_group0() {
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Zero, computed from four registers: an address offset by it cannot be used
+// until the loads that produced those registers have returned.  Used before
+// releasing a ring slot whose contents were loaded but are consumed only by
+// plain arithmetic (an arrive issued while such loads are in flight lets the
+// slot's next fill overwrite the data before they read it).
+__device__ __forceinline__ uint32_t zero_after(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    uint32_t z;
+    asm volatile(
+        "{\n\t.reg .b32 t;\n\t"
+        "or.b32 t, %1, %2;\n\t"
+        "or.b32 t, t, %3;\n\t"
+        "or.b32 t, t, %4;\n\t"
+        "and.b32 %0, t, 0;\n\t}"
+        : "=r"(z)
+        : "r"(a), "r"(b), "r"(c), "r"(d));
+    return z;
+}
+
 // Named barrier that also returns the AND of `pred` over the participating threads.
 __device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads, bool pred) {
     uint32_t r;

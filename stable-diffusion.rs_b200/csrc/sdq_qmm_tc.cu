@@ -281,7 +281,6 @@ __global__ void __launch_bounds__(512, 1)
                 const uint8_t* wrow = sW + ws * C::W_STAGE + r * C::W_ROW;
 #pragma unroll
                 for (int v = 0; v < NV; ++v) q[v] = *reinterpret_cast<const uint4*>(wrow + 16 * (v ^ sw));
-                mbar_arrive(wempty + ws);                     // the words are in registers
                 if (!mbar_wait_warp(done + as, ((it / SA) & 1) ^ 1, abort_flag, status, 4u)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t a[32];
@@ -316,6 +315,11 @@ __global__ void __launch_bounds__(512, 1)
                 tc_wait_st();
                 tc_fence_before();
                 mbar_arrive(ready + as);
+                // The packed slot is released only now: the tensor-memory store above
+                // consumed the words read from it, so those reads have returned.  An
+                // arrive right after the reads let the slot's next TMA fill overwrite it
+                // before they returned (seen as corrupt rows when the unpacking is slow).
+                mbar_arrive(wempty + ws);
             }
         }
     } else if (warp >= 8) {

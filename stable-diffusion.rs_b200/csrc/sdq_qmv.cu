@@ -295,8 +295,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         wb[u][0] = p1.x; wb[u][1] = p1.y; wb[u][2] = p1.z; wb[u][3] = p1.w;
                     }
                 }
-                __syncwarp();
-                if (last && lane == 0) mbar_arrive(wempty + s);
                 // Per-group X sums of tokens 2t and 2t + 1 for the U steps.
                 float xg[2 * C::U];
                 if (C::U == 2) {
@@ -351,6 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc[2] = fmaf(sf1, T[2], fmaf(bo1, xg[2 * u], acc[2]));
                     acc[3] = fmaf(sf1, T[3], fmaf(bo1, xg[2 * u + 1], acc[3]));
                 }
+                // Release the stage only once its words (read by the MMAs above) and its
+                // scales (tied in through zero_after) have been read back.
+                const uint32_t dep = zero_after(sr[0], sr[1], sr[2], sr[3]);
+                __syncwarp();
+                if (last && lane == 0) mbar_arrive(wempty + s + dep);
             }
             // A warp that gave up still reaches the barrier; the vote makes the
             // whole slice leave together.
