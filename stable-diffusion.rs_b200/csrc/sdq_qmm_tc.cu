@@ -7,7 +7,8 @@
 // The kernel computes the transposed tile D[f, t] = W_dq[f, :] . X[t, :]^T with
 //   * A = the dequantised weight tile, 128 features x 64 k, written straight
 //     into TENSOR MEMORY by the dequant warpgroups (tcgen05.st) -- it never
-//     passes through shared memory;
+//     passes through shared memory (an A ring in shared memory was tried: the
+//     extra 32 KB of shared traffic per step made it slower);
 //   * B = the activation tile, BT tokens x 64 k bf16 in shared memory with
 //     128-byte swizzle (loaded per step by TMA, or -- for BT = 16 when X fits
 //     -- loaded whole by TMA at kernel start and kept resident; rows >= M
@@ -28,17 +29,16 @@
 //   warp 0      TMA producer of the X ring (or of the resident X)
 //   warp 1      TMEM allocator and MMA issuer
 //   warp 2      TMA producer of the W ring
-//   warps 4-7   dequant warpgroup; thread r owns feature row r of the tile
-//   warps 8-15  epilogue, two warpgroups taking alternate 32-token chunks of
-//               the accumulator: TMEM -> registers (+bias, packed to bf16),
-//               release the accumulator, then store to global
-// Exactly one warp stores to each TMEM sub-partition (lanes 32w..32w+31).  With
-// two dequant warpgroups taking alternate steps -- two warps of one SM
-// sub-partition storing different columns of the same TMEM lanes at the same
-// time -- the MMAs occasionally read A columns that one warp's completed,
-// waited-for store had not yet made visible; one storing warp per
-// sub-partition never showed it, and costs nothing here (the single MMA-issuing
-// thread, not the unpacking, bounds the step rate).
+//   warps 4-11  two dequant warpgroups taking alternate steps of each tile;
+//               thread r of a group owns feature row r (TMEM lane r), so both
+//               groups store, into different A slots, the same TMEM lanes
+//   warps 12-15 epilogue: 32-token chunks of the accumulator -> registers
+//               (+bias, packed to bf16) -> shared staging -> TMA tensor store,
+//               with the accumulator released as soon as it has been read
+// A packed-weight slot is released only after the words read from it have been
+// consumed (stored to TMEM): releasing it right after the shared-memory reads let
+// the slot's next TMA fill land before those reads returned, which showed up as
+// intermittently corrupt rows whenever the unpacking ran slower than the copies.
 // Every mbarrier wait is bounded (2 s); on expiry the kernel records a status
 // bit, drains its own copies and MMAs, frees TMEM and returns.
 #include <cstdint>
@@ -58,6 +58,12 @@ namespace sdq {
 __device__ unsigned int g_tc_status = 0;
 
 namespace {
+
+// Dequant warpgroups (each takes every other group of K of a tile) and epilogue
+// warpgroups; with the four role warps they make 16 warps.
+constexpr int kDqGroups = 2;
+constexpr int kEpiGroups = 1;
+constexpr int kFirstEpiWarp = 4 + 4 * kDqGroups;
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 struct TcCfg {
@@ -106,7 +112,7 @@ __global__ void __launch_bounds__(512, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sY + C::Y_STAGE);
     // Step s uses X slot s % SX, W slot s % SW and A slot / barrier pair s % SA.
     //   wfull[w]   packed W landed                       count 1 + tx
-    //   wempty[w]  the dequant group read W slot w        count 128
+    //   wempty[w]  the dequant group of the step read W slot w   count 128
     //   ready[a]   A slot written and X landed: 128 dequant arrivals, plus (with an
     //              X ring) the X producer's arrive + expect-tx, completed by the
     //              bulk copy itself -- so the MMA warp observes the copy directly
@@ -117,7 +123,7 @@ __global__ void __launch_bounds__(512, 1)
     uint64_t* ready = wempty + SW;
     uint64_t* done = ready + SA;
     uint64_t* dfull = done + SA;             // accumulator complete       count 1 (commit)
-    uint64_t* dempty = dfull + 1;            // accumulator drained        count 256
+    uint64_t* dempty = dfull + 1;            // accumulator drained        count 128 per epilogue group
     uint64_t* drain = dfull + 2;             // abort drain of the MMA pipe
     uint64_t* xfull = dfull + 3;             // resident X landed          count 1 + tx
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 1);
@@ -131,7 +137,7 @@ __global__ void __launch_bounds__(512, 1)
         for (int i = 0; i < SW; ++i) { mbar_init(wfull + i, 1); mbar_init(wempty + i, 128); }
         for (int i = 0; i < SA; ++i) { mbar_init(ready + i, XRES ? 128 : 129); mbar_init(done + i, 1); }
         mbar_init(dfull, 1);
-        mbar_init(dempty, 256);
+        mbar_init(dempty, 128 * kEpiGroups);
         mbar_init(drain, 1);
         mbar_init(xfull, 1);
         *abort_flag = 0;
@@ -246,9 +252,12 @@ __global__ void __launch_bounds__(512, 1)
             tc_commit_elect(drain);
             mbar_wait_drain(drain, 0);
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < kFirstEpiWarp) {
         // ------------------------------------------------------------ dequant
-        const int r = threadIdx.x - 128;                      // feature row in the tile
+        // Group g unpacks the steps kt = g, g + kDqGroups, ... of every tile; the two
+        // groups store different A slots of the same TMEM lanes.
+        const int g = (warp - 4) >> 2;
+        const int r = (threadIdx.x - 128) & 127;              // feature row in the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const int G = K / 64;
         // The packed tile was written by TMA with a 32-byte (W4) / 64-byte (W8)
@@ -267,12 +276,15 @@ __global__ void __launch_bounds__(512, 1)
             // afterwards, so the warp never diverges ahead of its .aligned TMEM ops.
             // The next step's scale and bias are loaded while this one is unpacked.
             const uint32_t vmask = valid ? 0xFFFFu : 0u;
-            uint32_t sb_next = (uint32_t)__ldg(srow) & vmask;
-            uint32_t bb_next = (uint32_t)__ldg(brow) & vmask;
-            for (int kt = 0; kt < KT; ++kt, ++it) {
+            const int kfirst = g < KT ? g : KT - 1;
+            uint32_t sb_next = (uint32_t)__ldg(srow + kfirst) & vmask;
+            uint32_t bb_next = (uint32_t)__ldg(brow + kfirst) & vmask;
+            const int it0 = it;                                // the tile's first step
+            for (int kt = g; kt < KT; kt += kDqGroups) {
+                it = it0 + kt;
                 const int ws = it % SW, as = it % SA;
                 const uint32_t sb = sb_next, bb = bb_next;
-                const int kn = kt + 1 < KT ? kt + 1 : kt;
+                const int kn = kt + kDqGroups < KT ? kt + kDqGroups : kt;
                 sb_next = (uint32_t)__ldg(srow + kn) & vmask;
                 bb_next = (uint32_t)__ldg(brow + kn) & vmask;
                 if (!mbar_wait_warp(wfull + ws, (it / SW) & 1, abort_flag, status, 4u)) { ok = false; break; }
@@ -321,20 +333,21 @@ __global__ void __launch_bounds__(512, 1)
                 // before they returned (seen as corrupt rows when the unpacking is slow).
                 mbar_arrive(wempty + ws);
             }
+            it = it0 + KT;
         }
-    } else if (warp >= 8) {
+    } else if (warp >= kFirstEpiWarp) {
         // ------------------------------------------------------------ epilogue
-        // Group e takes chunks e, e + 2, ... (32 tokens; one 16-token chunk when
-        // BT = 16): TMEM -> registers (+bias) -> bf16 into the shared staging tile
-        // [token][feature].  The accumulator is released as soon as both groups
-        // have read it.  Then one thread per group writes each chunk with a TMA
+        // Group e takes chunks e, e + kEpiGroups, ... (32 tokens; one 16-token chunk
+        // when BT = 16): TMEM -> registers (+bias) -> bf16 into the shared staging
+        // tile [token][feature].  The accumulator is released as soon as every
+        // group has read it.  Then one thread per group writes each chunk with a TMA
         // tensor store, which clips tokens >= M and features >= N; when Y's row
         // pitch or base is not 16-byte aligned the group copies the chunk with
         // plain stores instead.  A timed-out wait is made group-uniform by the
         // reducing barrier, so no warp of the group is left at a named barrier.
         constexpr int CW = BT < 32 ? BT : 32;             // tokens per chunk
         constexpr int NCH = BT / CW;                      // chunks per tile
-        const int e = (warp - 8) >> 2;
+        const int e = (warp - kFirstEpiWarp) >> 2;
         const int fl = 32 * (warp & 3) + lane;            // feature row within the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const bool leader = (warp & 3) == 0 && lane == 0;
@@ -351,7 +364,7 @@ __global__ void __launch_bounds__(512, 1)
                                        mbar_wait_sleep(dfull, tc & 1, abort_flag, status, 8u, 64));
             if (ok) {
                 tc_fence_after();
-                for (int c = e; c < NCH; c += 2) {
+                for (int c = e; c < NCH; c += kEpiGroups) {
                     uint16_t* yrow = reinterpret_cast<uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
 #pragma unroll
                     for (int h = 0; h < CW / 16; ++h) {
@@ -373,14 +386,14 @@ __global__ void __launch_bounds__(512, 1)
             if (!named_barrier_and(1 + e, 128, ok)) break;
             if (y_tma) {
                 if (leader) {
-                    for (int c = e; c < NCH; c += 2)
+                    for (int c = e; c < NCH; c += kEpiGroups)
                         if (tt * BT + c * CW < M)
                             tma_store_2d(&tmY, sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
                                          tt * BT + c * CW);
                     bulk_commit_group();
                 }
             } else if (f < N) {
-                for (int c = e; c < NCH; c += 2) {
+                for (int c = e; c < NCH; c += kEpiGroups) {
                     const uint16_t* yrow =
                         reinterpret_cast<const uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
                     const int t0 = tt * BT + c * CW;
