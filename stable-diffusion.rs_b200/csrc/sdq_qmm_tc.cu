@@ -25,14 +25,15 @@
 //   A ring  (SA slots in TMEM)  dequant      -> MMA
 // so the weight stream and its unpacking run many steps ahead of the MMAs.
 //
-// Warp roles (512 threads, one CTA per SM, persistent over tiles):
+// Warp roles (640 threads for W4, 512 for W8; one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of the X ring (or of the resident X)
 //   warp 1      TMEM allocator and MMA issuer
 //   warp 2      TMA producer of the W ring
-//   warps 4-11  two dequant warpgroups taking alternate steps of each tile;
-//               thread r of a group owns feature row r (TMEM lane r), so both
-//               groups store, into different A slots, the same TMEM lanes
-//   warps 12-15 epilogue: 32-token chunks of the accumulator -> registers
+//   warps 4-..  dequant warpgroups (three for W4, two for W8) taking the steps
+//               of each tile in turn; thread r of a group owns feature row r
+//               (TMEM lane r), so the groups store, into different A slots, the
+//               same TMEM lanes
+//   last 4      epilogue: 32-token chunks of the accumulator -> registers
 //               (+bias, packed to bf16) -> shared staging -> TMA tensor store,
 //               with the accumulator released as soon as it has been read
 // A packed-weight slot is released only after the words read from it have been
@@ -59,11 +60,14 @@ __device__ unsigned int g_tc_status = 0;
 
 namespace {
 
-// Dequant warpgroups (each takes every other group of K of a tile) and epilogue
-// warpgroups; with the four role warps they make 16 warps.
-constexpr int kDqGroups = 2;
+// Dequant warpgroups (group g takes the groups of K with kt % DQ == g) and one
+// epilogue warpgroup.  W4 runs three dequant groups (20 warps: its unpacking is the
+// longer half of a step and its registers allow 640 threads); W8 runs two (16
+// warps), its unpacking needing more registers than 640 threads leave.
 constexpr int kEpiGroups = 1;
-constexpr int kFirstEpiWarp = 4 + 4 * kDqGroups;
+__host__ __device__ constexpr int dq_groups(int bits) { return bits == 4 ? 3 : 2; }
+__host__ __device__ constexpr int first_epi_warp(int bits) { return 4 + 4 * dq_groups(bits); }
+__host__ __device__ constexpr int tc_threads(int bits) { return 32 * (first_epi_warp(bits) + 4 * kEpiGroups); }
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 struct TcCfg {
@@ -74,7 +78,8 @@ struct TcCfg {
     static constexpr int W_STAGE = BF * W_ROW;
     static constexpr int W_WORDS = BK * BITS / 32;         // packed words per row per step
     static constexpr uint32_t D_COL = 0;                   // accumulator columns [0, BT)
-    static constexpr uint32_t A_COL = BT < 32 ? 32 : BT;   // A slots: 32 columns each
+    static constexpr uint32_t A_COL = (BT + 31) / 32 * 32; // A slots: 32 columns each
+    static constexpr int CW = BT % 32 == 0 ? 32 : 16;      // tokens per epilogue chunk
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr int Y_STAGE = BT * BF * 2;            // bf16 staging of one output tile
     static constexpr int RING_BYTES = (XRES ? 0 : SX * X_STAGE) + SW * W_STAGE + Y_STAGE;
@@ -93,7 +98,7 @@ size_t smem_bytes(int64_t k) {
 }
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(tc_threads(BITS), 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmY,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
@@ -252,10 +257,11 @@ __global__ void __launch_bounds__(512, 1)
             tc_commit_elect(drain);
             mbar_wait_drain(drain, 0);
         }
-    } else if (warp >= 4 && warp < kFirstEpiWarp) {
+    } else if (warp >= 4 && warp < first_epi_warp(BITS)) {
         // ------------------------------------------------------------ dequant
-        // Group g unpacks the steps kt = g, g + kDqGroups, ... of every tile; the two
-        // groups store different A slots of the same TMEM lanes.
+        // Group g unpacks the steps kt = g, g + DQ, ... of every tile; the groups
+        // store different A slots of the same TMEM lanes.
+        constexpr int kDqGroups = dq_groups(BITS);
         const int g = (warp - 4) >> 2;
         const int r = (threadIdx.x - 128) & 127;              // feature row in the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -335,7 +341,7 @@ __global__ void __launch_bounds__(512, 1)
             }
             it = it0 + KT;
         }
-    } else if (warp >= kFirstEpiWarp) {
+    } else if (warp >= first_epi_warp(BITS)) {
         // ------------------------------------------------------------ epilogue
         // Group e takes chunks e, e + kEpiGroups, ... (32 tokens; one 16-token chunk
         // when BT = 16): TMEM -> registers (+bias) -> bf16 into the shared staging
@@ -345,9 +351,9 @@ __global__ void __launch_bounds__(512, 1)
         // pitch or base is not 16-byte aligned the group copies the chunk with
         // plain stores instead.  A timed-out wait is made group-uniform by the
         // reducing barrier, so no warp of the group is left at a named barrier.
-        constexpr int CW = BT < 32 ? BT : 32;             // tokens per chunk
+        constexpr int CW = C::CW;                         // tokens per chunk
         constexpr int NCH = BT / CW;                      // chunks per tile
-        const int e = (warp - kFirstEpiWarp) >> 2;
+        const int e = (warp - first_epi_warp(BITS)) >> 2;
         const int fl = 32 * (warp & 3) + lane;            // feature row within the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const bool leader = (warp & 3) == 0 && lane == 0;
@@ -466,7 +472,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     if (y_tma) {
         cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
         cuuint64_t strides[1] = {(cuuint64_t)n * 2};
-        cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)(BT < 32 ? BT : 32)};
+        cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)C::CW};
         cuuint32_t estr[2] = {1, 1};
         CUresult r = enc(&tmY, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -489,7 +495,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     }
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, 512, smem, st>>>(
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), static_cast<const uint16_t*>(bias),
         static_cast<uint16_t*>(y), (int)m, (int)n, (int)k, y_tma ? 1 : 0);
@@ -500,8 +506,13 @@ template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                            const void* scales, const void* biases, int64_t n, const void* bias,
                            void* y, cudaStream_t st, const char** msg) {
-    // Tokens per tile: the smallest of 16 / 64 / 128 / 256 that covers M, so short
-    // activations do not pay for empty MMA columns.  Ring depths fill the shared
+    // Tokens per tile.  Up to 128 tokens: the smallest of 16 / 64 / 128 that covers
+    // M, so short activations do not pay for empty MMA columns.  Beyond that the
+    // tile height is chosen so the tiles fill whole waves of the SMs: cost = waves x
+    // (per-step time + a fixed per-tile share), the step time being the MMA's (BT
+    // tokens) or the unpacking's (about 128 tokens' worth for W4, 288 for W8),
+    // whichever is longer.  1024 x 3072 output at W4 thus runs as 144 tiles of 176
+    // tokens in one wave instead of 96 tiles of 256.  Ring depths fill the shared
     // memory budget; the packed-weight ring is the deep one.
     constexpr int SWs = BITS == 4 ? 16 : 12;
     using CR = TcCfg<BITS, 16, 1, SWs, 14, true>;
@@ -509,9 +520,27 @@ cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* 
         return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
     if (m <= 16) return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
     if (m <= 64) return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    if (m <= 128) return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    constexpr int SW256 = BITS == 4 ? 8 : 4;
-    return launch_tc_t<BITS, 256, 4, SW256, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    constexpr int SWL = BITS == 4 ? 8 : 4;
+    int bt = 128;
+    if (m > 128) {
+        const int64_t sms = num_sms(), nft = (n + 127) / 128;
+        const int64_t dq = BITS == 4 ? 128 : 288, fixed = 32;
+        int64_t best = -1;
+        for (int cand : {128, 176, 240, 256}) {
+            const int64_t tiles = (m + cand - 1) / cand * nft;
+            const int64_t cost = (tiles + sms - 1) / sms * ((cand > dq ? cand : dq) + fixed);
+            if (best < 0 || cost <= best) {                // ties go to the taller tile
+                best = cost;
+                bt = cand;
+            }
+        }
+    }
+    switch (bt) {
+        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    }
 }
 
 }  // namespace

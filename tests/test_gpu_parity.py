@@ -173,10 +173,12 @@ def test_small_m_long_k(m, k, bits):
     assert_close(y, want, f"m={m} k={k} bits={bits}")
 
 
-@pytest.mark.parametrize("bits,k,n", [(4, 3072, 18432), (8, 12288, 3072)])
+@pytest.mark.parametrize("bits,k,n", [(4, 3072, 18432), (8, 12288, 3072),
+                                      (4, 1024, 3072), (4, 4096, 3072), (8, 1024, 3072)])
 def test_identity_activation_reproduces_the_dequantised_weight(bits, k, n):
     """Full-size property: X = I (M = K) gives Y = dequant(W)^T exactly, since each output is
-    one exact product; checks the tensor-core path against the dequantise kernel bit for bit."""
+    one exact product; checks the tensor-core path against the dequantise kernel bit for bit.
+    M = 1024 and 4096 against N = 3072 select the 176- and 240-token tiles."""
     w = torch.randn(n, k, device="cuda", generator=torch.Generator("cuda").manual_seed(bits)) * 0.02
     wq, s, b = sdq.quantize(w, 64, bits)
     eye = torch.eye(k, device="cuda", dtype=torch.bfloat16)
