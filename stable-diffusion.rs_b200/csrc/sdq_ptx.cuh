@@ -167,7 +167,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 // 2-D tiled load global -> shared, completion counted on `bar` in bytes.
-// No multicast: every CTA loads its own tiles.
+// Every CTA loads its own tiles; no copy is shared between CTAs.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tmap, uint64_t* bar,
                                             int32_t c0, int32_t c1) {
     asm volatile(
@@ -177,7 +177,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
         : "memory");
 }
 // 1-D bulk copy global -> shared of `bytes` (a multiple of 16; both addresses
-// 16-byte aligned), completion counted on `bar` in bytes.  No multicast.
+// 16-byte aligned), completion counted on `bar` in bytes; this CTA only.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
     asm volatile(
