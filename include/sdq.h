@@ -149,6 +149,27 @@ int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, in
                                  const void* bias_local, void* y_shards, void* y,
                                  sdq_dtype y_dtype, void* comm, void* stream);
 
+/*
+ * sdq_quantized_matmul_sharded without the caller's y_shards buffer, for callers
+ * that cannot allocate device memory when they call it (an engine whose arena
+ * owns all of HBM from start-up, a loop that may not stall on cudaFree).  The
+ * [world, m, n_local] all-gather buffer is a static 8 MiB device array inside
+ * the library, held on every GPU that loads it until the process exits, so
+ * world*m*n_local must not exceed 4 Mi bf16 values (larger calls return
+ * SDQ_ERR_INVALID naming the limit).  y must be non-NULL.  The call itself
+ * allocates nothing; NCCL's buffers belong to the communicator.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the array: each
+ * call writes every element it reads, so nothing needs clearing, but calls whose
+ * work overlaps on the GPU (other streams, other host threads) race on it.
+ * No counterpart in the reference: its matmul allocates through MLX.
+ */
+int sdq_quantized_matmul_sharded_static(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                                        const uint32_t* wq, const void* scales, const void* biases,
+                                        sdq_dtype sb_dtype, int64_t n_local, int group_size,
+                                        int bits, const void* bias_local, void* y,
+                                        sdq_dtype y_dtype, void* comm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,8 +4,10 @@
 // weight), runs the single-GPU kernel on it, and the [m, n_local] results are
 // all-gathered over NVLink / NVSwitch.  NCCL's all-gather concatenates rank
 // chunks, so a permute kernel turns [world, m, n_local] into [m, n].
-#include <cstring>
 #include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -157,6 +159,88 @@ int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, in
         }
     }
     return sdq::set_error_message(SDQ_OK, "");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers cannot allocate device memory when they call the sharded linear: an
+// engine that hands all of HBM to its own arena at start-up (cudaMalloc would then
+// fail, or escape its accounting), or a host loop that must not stall (cudaFree
+// synchronises the whole device).  For them the [world, m, n_local] all-gather
+// buffer lives in this file-scope array instead of a caller buffer.  It costs
+// kStaticShardBytes of device memory on every GPU that loads the library, for as
+// long as the process runs, and bounds world * m * n_local.
+namespace {
+
+constexpr size_t kStaticShardBytes = size_t(8) << 20;                // 8 MiB
+constexpr size_t kStaticShardElems = kStaticShardBytes / sizeof(uint16_t);
+
+static __device__ __align__(256) uint16_t g_static_shards[kStaticShardElems];
+
+// The array's device address on each device, fetched once with that device current.
+// In host code the name g_static_shards is only a host-side stand-in; kernels and
+// NCCL must be given this address.
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+
+cudaError_t static_shards_on_current_device(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_shards);
+        if (e != cudaSuccess) return e;
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return cudaSuccess;
+}
+
+thread_local char t_static_msg[256];
+
+}  // namespace
+
+extern "C" {
+
+int sdq_quantized_matmul_sharded_static(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                                        const uint32_t* wq, const void* scales, const void* biases,
+                                        sdq_dtype sb_dtype, int64_t n_local, int group_size,
+                                        int bits, const void* bias_local, void* y,
+                                        sdq_dtype y_dtype, void* comm, void* stream) {
+    const char* fn = "sdq_quantized_matmul_sharded_static";
+    if (!comm || !y) {
+        std::snprintf(t_static_msg, sizeof t_static_msg, "%s: comm and y must be non-null", fn);
+        return sdq::set_error_message(SDQ_ERR_INVALID, t_static_msg);
+    }
+    if (m <= 0 || n_local <= 0) {
+        std::snprintf(t_static_msg, sizeof t_static_msg, "%s: m and n_local must be >= 1", fn);
+        return sdq::set_error_message(SDQ_ERR_INVALID, t_static_msg);
+    }
+    const Comm* c = static_cast<const Comm*>(comm);
+    const double need = static_cast<double>(c->world) * static_cast<double>(m) *
+                        static_cast<double>(n_local);
+    if (need > static_cast<double>(kStaticShardElems)) {
+        std::snprintf(t_static_msg, sizeof t_static_msg,
+                      "%s: world*m*n_local = %.0f bf16 values exceeds the static scratch of %zu "
+                      "(%zu MiB); use sdq_quantized_matmul_sharded with a caller buffer",
+                      fn, need, kStaticShardElems, kStaticShardBytes >> 20);
+        return sdq::set_error_message(SDQ_ERR_INVALID, t_static_msg);
+    }
+    void* scratch = nullptr;
+    const cudaError_t e = static_shards_on_current_device(&scratch);
+    if (e != cudaSuccess) {
+        std::snprintf(t_static_msg, sizeof t_static_msg,
+                      "%s: cudaGetSymbolAddress of the static scratch: %s", fn, cudaGetErrorString(e));
+        return sdq::set_error_message(SDQ_ERR_CUDA, t_static_msg);
+    }
+    return sdq_quantized_matmul_sharded(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n_local,
+                                        group_size, bits, bias_local, scratch, y, y_dtype, comm,
+                                        stream);
 }
 
 }  // extern "C"

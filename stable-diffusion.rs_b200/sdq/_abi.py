@@ -40,6 +40,8 @@ SIGNATURES = {
     "sdq_comm_destroy": (_i32, [_p]),
     "sdq_quantized_matmul_sharded": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32,
                                             _p, _p, _p, _i32, _p, _p]),
+    "sdq_quantized_matmul_sharded_static": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32,
+                                                   _i32, _p, _p, _i32, _p, _p]),
 }
 
 

@@ -1,0 +1,81 @@
+"""The sharded linear's entry point that allocates nothing: sdq_quantized_matmul_sharded_static.
+
+It exists for callers that cannot allocate device memory when they call the linear -- an
+engine whose own arena holds all of HBM from start-up, or a loop that must not stall on
+cudaFree -- and keeps the all-gather buffer in an 8 MiB array inside the library instead
+of taking one from the caller.  These tests call it through the C ABI and compare it with
+sdq_quantized_matmul_sharded (the caller-buffer entry point), on two calls in a row since
+every call reuses the same array.  The file is named so that pytest collects it last; it
+also passes on its own in a fresh process.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import sdq
+from sdq import _abi
+from conftest import gpu_available
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not gpu_available(), reason="needs an sm_100 device")]
+
+MAX_ABS_REL = 1e-2          # the matmul tolerance used by every parity test
+MIN_COSINE = 0.9999
+LIMIT = (8 << 20) // 2      # bf16 values the static array holds
+
+
+def _close(got: torch.Tensor, want: torch.Tensor):
+    g, w = got.double(), want.double()
+    rel = float((g - w).abs().max() / w.abs().max().clamp_min(1e-30))
+    cos = float((g * w).sum() / (g.norm() * w.norm()).clamp_min(1e-300))
+    return rel, cos
+
+
+def _static(x, wq, s, b, comm, bits, y, bias=None) -> int:
+    m, k = x.shape
+    return _abi.lib().sdq_quantized_matmul_sharded_static(
+        ctypes.c_void_p(x.data_ptr()), _abi.SDQ_BF16, m, k, ctypes.c_void_p(wq.data_ptr()),
+        ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(b.data_ptr()), _abi.SDQ_BF16, wq.shape[0], 64,
+        bits, ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
+        ctypes.c_void_p(y.data_ptr()), _abi.SDQ_BF16, comm.handle,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m,k,n", [(300, 256, 1000), (4, 512, 3072)])
+def test_static_scratch_matches_the_caller_buffer_entry_point_on_two_calls(bits, m, k, n):
+    g = torch.Generator("cuda").manual_seed(41 + bits)
+    wq, s, b = sdq.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02, 64, bits)
+    bias = (torch.randn(n, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    comm = sdq.Comm(sdq.Comm.unique_id(), 1, 0)
+    try:
+        for call in range(2):
+            x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+            want, _ = sdq.quantized_matmul_sharded(x, wq, s, b, comm, 64, bits, bias=bias)
+            y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
+            _abi.check(_static(x, wq, s, b, comm, bits, y, bias))
+            sdq.device_status()
+            rel, cos = _close(y, want)
+            assert rel <= MAX_ABS_REL and cos >= MIN_COSINE, (
+                f"call {call}: max-abs-rel {rel:.3e}, cosine {cos:.7f}")
+    finally:
+        comm.destroy()
+
+
+def test_static_scratch_rejects_sizes_beyond_its_limit():
+    m, k, n = 4096, 64, 2048           # 8 Mi values: twice what the array holds
+    assert m * n > LIMIT
+    x = torch.zeros(m, k, device="cuda", dtype=torch.bfloat16)
+    wq, s, b = sdq.quantize(torch.zeros(n, k, device="cuda"), 64, 4)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    comm = sdq.Comm(sdq.Comm.unique_id(), 1, 0)
+    try:
+        rc = _static(x, wq, s, b, comm, 4, y)
+        msg = _abi.last_error()             # read before a later successful call clears it
+    finally:
+        comm.destroy()
+    assert rc == _abi.SDQ_ERR_INVALID
+    assert "static scratch" in msg
