@@ -9,6 +9,10 @@ Workloads (the benchmark plan's configurations; data synthetic, seeded):
   cfg1  X [1024, 3072] . W [3072, 3072]^T, W4
   cfg3  X [M<=8, 3072] . W [18432, 3072]^T, W4 (HBM-bound; reports GB/s)
   cfg5  X [16384, 3072] . W [12288, 3072]^T, W4
+  cfg4  the Flux-shaped stack (sdq.flux): 312 linears of one transformer forward (19 double +
+        38 single blocks, 512 text + 4096 image tokens, out-proj / MLP down-proj W8, rest W4);
+        a step replays the forward's linears as one CUDA graph (value), and the whole forward
+        (attention and elementwise work included) is timed beside it
 A step is one quantised matmul over the workload's X with the weight resident in HBM.
 With N > 1 ranks each rank holds one workload-sized column shard of a weight N times
 as wide (weak scaling) and the [M, N*n] output is all-gathered over NVLink (NCCL).
@@ -128,6 +132,8 @@ def cpu_reference(args, wl):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
+    if wl == "cfg4":
+        return cpu_reference_flux(args, O)
     m, k, n, bits, sig, kind = WORKLOADS[wl]
     threads = O.max_threads()
     ms = min(m, 8 if kind == "gbs" else 48)     # sample rows of X per step
@@ -148,12 +154,155 @@ def cpu_reference(args, wl):
     return value, threads, sample
 
 
+def cpu_reference_flux(args, O):
+    """The oracle over a sample of the Flux stack's linears: 16 rows of X through each distinct
+    linear shape of a double block, a single block and a modulation, in TFLOP/s."""
+    threads = O.max_threads()
+    shapes = [(9216, 3072, 4), (3072, 3072, 8), (12288, 3072, 4), (3072, 12288, 8),
+              (21504, 3072, 4), (3072, 15360, 8), (18432, 3072, 4)]
+    ms = 16
+    cases = []
+    for i, (n, k, bits) in enumerate(shapes):
+        xb, w = O.synthetic_linear(500 + i, ms, k, n, 1.0 / k ** 0.5)
+        cases.append((xb, O.quantize(w, bits), n, bits, 2.0 * ms * n * k))
+    times = []
+    for it in range(1 + args.steps):
+        t0 = time.perf_counter()
+        for xb, (wq, s, b), n, bits, _ in cases:
+            O.qmatmul(xb, wq, s, b, n, bits, threads=threads)
+        if it:
+            times.append(time.perf_counter() - t0)
+    flops = sum(c[4] for c in cases)
+    t = statistics.median(times)
+    sample = f"16 rows of X through each of {len(shapes)} Flux linear shapes (W4/W8); median of {len(times)}"
+    return flops / t / 1e12, threads, sample
+
+
+def run_flux(args, rank, world, local):
+    """Config 4: one forward of the Flux-shaped stack, every linear through libsdq.  N > 1 runs
+    independent replicas (the stack does not shard here); the time is the max over ranks."""
+    import torch
+    import sdq
+    from sdq import flux
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    cfg = flux.FluxShape()
+    total_flops = flux.flops(cfg)
+    qw = flux.random_weights(cfg, seed=11, device=dev)
+    rope = flux.rope_tables(cfg, device=dev)
+    ins = flux.inputs(cfg, seed=12, device=dev)
+    lin = flux.LinearsOnly(qw, cfg, seed=13, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up eagerly (first calls configure every kernel variant), then capture both passes
+    for _ in range(args.warmup):
+        lin()
+        flux.forward(qw, *ins, cfg, rope)
+    sdq.device_status()
+    g_lin, g_fwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_lin):
+        lin()
+    with torch.cuda.graph(g_fwd):
+        out = flux.forward(qw, *ins, cfg, rope)
+    for _ in range(2):
+        g_lin.replay()
+        g_fwd.replay()
+    barrier()
+    sdq.device_status()
+
+    def timed(fn, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        barrier()
+        t = sum(a.elapsed_time(b) for a, b in ev)
+        if dist is not None:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t / steps
+
+    with ClockSampler(local) as clk:
+        lin_ms = timed(g_lin.replay, args.steps)
+    fwd_ms = timed(g_fwd.replay, args.steps)
+    sdq.device_status()
+
+    # end to end: the eager forward through the public API with host inputs and output
+    hosts = [t.cpu().pin_memory() for t in ins]
+    devs = [torch.empty_like(t) for t in ins]
+    oh = torch.empty(tuple(out.shape), dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        o = flux.forward(qw, *devs, cfg, rope)
+        oh.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = timed(e2e_step, max(2, args.steps // 2))
+
+    value = total_flops * world / (lin_ms * 1e-3) / 1e12
+    hbm, tc, src = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cv, threads, sample = cpu_reference(argparse.Namespace(steps=3, warmup=3), "cfg4")
+        cpu = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        achieved = total_flops / (lin_ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "qmatmul_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": lin_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init Flux-shaped weights, quantised by libsdq)",
+            "config": {"workload": "cfg4",
+                       "descr": "config 4: Flux-schnell-shaped stack, 19 double + 38 single blocks, "
+                                "512 txt + 4096 img tokens, hidden 3072, out-proj/MLP-down W8, rest W4",
+                       "linears": len(flux.linear_table(cfg)), "qmm_tflop_per_forward": total_flops / 1e12,
+                       "packed_weight_bytes": qw.resident_bytes(),
+                       "forward_ms": fwd_ms, "qmm_share_of_forward": lin_ms / fwd_ms,
+                       "parallelism": "single GPU" if world == 1 else f"{world} replicas",
+                       "l2": "weights (8.5 GB) exceed L2; 256 MiB write before every step anyway"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc, "unit": "TFLOP/s",
+                         "frac": achieved / tc, "peak_source": f"{src} burst bf16 (MEASURED_PEAKS.json)",
+                         "traffic": None, "kernel_ms": lin_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_flops * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in ins),
+                    "d2h_bytes_per_step": out.numel() * out.element_size(),
+                    "path": "sdq.flux.forward (every linear through the C ABI), host inputs in, output out"},
+            "gpu_launches": args.steps * len(flux.linear_table(cfg)),
+            "clocks": clk.summary(),
+        }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg2", choices=sorted(list(WORKLOADS) + ["cfg4"]))
     ap.add_argument("--impl", default="sdq", choices=["sdq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -163,7 +312,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     wl = args.workload
-    m, k, n, bits, sig, kind = WORKLOADS[wl]
+    kind = "tflops" if wl == "cfg4" else WORKLOADS[wl][5]
     metric = "qmatmul_tflops" if kind == "tflops" else "qmatmul_hbm_gbs"
     unit = "TFLOP/s" if kind == "tflops" else "GB/s"
 
@@ -175,12 +324,16 @@ def main():
             "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (SeededRng)",
-            "config": {"workload": wl, "descr": DESCR[wl], "parallelism": "host threads"},
+            "config": {"workload": wl, "descr": DESCR.get(wl, "config 4: Flux-shaped stack"),
+                       "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
         return
+    if wl == "cfg4":
+        return run_flux(args, rank, world, local)
+    m, k, n, bits, sig, kind = WORKLOADS[wl]
 
     import torch
     import sdq

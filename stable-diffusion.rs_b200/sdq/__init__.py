@@ -145,10 +145,12 @@ class QuantizedArray:
         return dequantize(self.weight, self.scales, self.biases, self.group_size, self.bits,
                           out_dtype, stream)
 
-    def matmul(self, x: torch.Tensor, bias: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-        """``x @ weight.T``, dequantising inside the kernel (mlx.rs:1947-1975)."""
+    def matmul(self, x: torch.Tensor, bias: torch.Tensor | None = None, stream=None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """``x @ weight.T``, dequantising inside the kernel (mlx.rs:1947-1975); ``out``, if
+        given, receives the result."""
         return quantized_matmul(x, self.weight, self.scales, self.biases, self.group_size, self.bits,
-                                bias=bias, stream=stream)
+                                bias=bias, out=out, stream=stream)
 
     def resident_bytes(self) -> int:
         """Bytes this weight occupies, counted as the reference does (4 bytes per scale)."""
