@@ -142,6 +142,11 @@ int sdq_comm_destroy(void* comm);
  * permutes that into y[m, world*n_local].  y_shards is caller-provided
  * (world*m*n_local elements, 16-byte aligned).  The compute step is
  * sdq_quantized_matmul; the exchange is one ncclAllGather on `stream`.
+ * When y is non-NULL, world > 1 and M spans several token tiles, the exchange
+ * instead overlaps the compute: finished row chunks are pushed by the copy
+ * engines into the peers' library-owned exchange buffers (allocated on the
+ * first such call, grown when a call needs more) and y_shards then holds only
+ * this rank's block on return.  Every rank must make the same calls.
  */
 int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                                  const uint32_t* wq, const void* scales, const void* biases,

@@ -116,6 +116,31 @@ int num_sms() {
 
 using namespace sdq;
 
+namespace sdq {
+// The argument checks of sdq_quantized_matmul, shared with the overlapped sharded path.
+int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
+                 const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n,
+                 int transpose, int& group_size, int& bits, const char* mode, const void* bias,
+                 const void* y, sdq_dtype y_dtype, const char* fn) {
+    int rc;
+    if ((rc = check_qparams(group_size, bits, mode, fn))) return rc;
+    if ((rc = check_nk(n, k, fn))) return rc;
+    if (m <= 0) return fail(SDQ_ERR_INVALID, "%s: m (rows of x) must be >= 1; got %lld", fn, (long long)m);
+    if (m > INT32_MAX) return fail(SDQ_ERR_INVALID, "%s: m must be < 2^31", fn);
+    if (!transpose)
+        return fail(SDQ_ERR_UNSUPPORTED,
+                    "%s: transpose=false is not supported (weights are [out, in]; pass true)", fn);
+    if (!x || !wq || !scales || !biases || !y)
+        return fail(SDQ_ERR_INVALID, "%s: x, wq, scales, biases and y must be non-null", fn);
+    if (x_dtype != SDQ_BF16 || y_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16", fn);
+    if (!aligned(x, 16) || !aligned(wq, 16) || !aligned(y, 2) || !aligned(scales, 2) ||
+        !aligned(biases, 2) || (bias && !aligned(bias, 2)))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
+    return check_device();
+}
+}  // namespace sdq
+
 extern "C" {
 
 const char* sdq_last_error(void) { return t_last_error.c_str(); }
@@ -184,21 +209,9 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                          void* y, sdq_dtype y_dtype, void* stream) {
     const char* fn = "sdq_quantized_matmul";
     int rc;
-    if ((rc = check_qparams(group_size, bits, mode, fn))) return rc;
-    if ((rc = check_nk(n, k, fn))) return rc;
-    if (m <= 0) return fail(SDQ_ERR_INVALID, "%s: m (rows of x) must be >= 1; got %lld", fn, (long long)m);
-    if (m > INT32_MAX) return fail(SDQ_ERR_INVALID, "%s: m must be < 2^31", fn);
-    if (!transpose)
-        return fail(SDQ_ERR_UNSUPPORTED,
-                    "%s: transpose=false is not supported (weights are [out, in]; pass true)", fn);
-    if (!x || !wq || !scales || !biases || !y)
-        return fail(SDQ_ERR_INVALID, "%s: x, wq, scales, biases and y must be non-null", fn);
-    if (x_dtype != SDQ_BF16 || y_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16)
-        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16", fn);
-    if (!aligned(x, 16) || !aligned(wq, 16) || !aligned(y, 2) || !aligned(scales, 2) ||
-        !aligned(biases, 2) || (bias && !aligned(bias, 2)))
-        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
-    if ((rc = check_device())) return rc;
+    if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, transpose,
+                                group_size, bits, mode, bias, y, y_dtype, fn)))
+        return rc;
     const char* msg = nullptr;
     bool taken = false;
     cudaError_t e = launch_qmv(x, m, k, wq, scales, biases, n, bits, bias, y,

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include "../../include/sdq.h"
+
 namespace sdq {
 
 // Streaming multiprocessors of the current device (cached per device).
@@ -29,6 +31,22 @@ cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,
                           const void* bias, void* y, cudaStream_t st, const char** msg);
+
+// The argument and device checks of sdq_quantized_matmul (status, message set on failure).
+int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
+                 const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n,
+                 int transpose, int& group_size, int& bits, const char* mode, const void* bias,
+                 const void* y, sdq_dtype y_dtype, const char* fn);
+
+// The tensor-core matmul for the overlapped sharded linear: the same kernel, on at most
+// grid_cap CTAs (0: every SM), adding 1 to done[tt / chunk_tts] once token tile tt's output
+// tile is in global memory (nchunks counters).  qmm_tc_tile_tokens is the token-tile height
+// the dispatcher picks for the shape.
+int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap);
+cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
+                                 const void* scales, const void* biases, int64_t n, int bits,
+                                 const void* bias, void* y, cudaStream_t st, const char** msg,
+                                 uint32_t* done, int chunk_tts, int nchunks, int grid_cap);
 
 // Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs).
 // Sets *taken = false, launching nothing, for shapes it does not serve (M > 8, or X too

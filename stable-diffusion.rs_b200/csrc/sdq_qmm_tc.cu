@@ -70,6 +70,18 @@ __host__ __device__ constexpr int first_epi_warp(int bits) { return 4 + 4 * dq_g
 __host__ __device__ constexpr int tc_threads(int bits) { return 32 * (first_epi_warp(bits) + 4 * kEpiGroups); }
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
+struct TcCfg;
+
+// Optional completion signal for overlapping the output's exchange with the compute:
+// token tile tt belongs to chunk tt / chunk_tts, and once a tile's Y is in global memory
+// the epilogue adds 1 to done[chunk].  done == nullptr turns it off.
+struct TcSignal {
+    uint32_t* done;
+    int chunk_tts;
+    int nchunks;
+};
+
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 struct TcCfg {
     static constexpr int BF = 128;                         // features per tile = MMA M
     static constexpr int BK = 64;                          // k per step = one group
@@ -103,7 +115,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                   const __grid_constant__ CUtensorMap tmY,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
                   const uint16_t* __restrict__ biases, const uint16_t* __restrict__ bias,
-                  uint16_t* __restrict__ y, int M, int N, int K, int y_tma) {
+                  uint16_t* __restrict__ y, int M, int N, int K, int y_tma, const TcSignal sig) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -407,6 +419,20 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                     for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * N + f] = yrow[r * C::BF];
                 }
             }
+            if (sig.done != nullptr) {
+                // This tile's Y must be in global memory before its chunk counts it.
+                if (y_tma) {
+                    if (leader) {
+                        bulk_wait_group0();
+                        __threadfence();
+                        atomicAdd(sig.done + tt / sig.chunk_tts, 1u);
+                    }
+                } else {
+                    __threadfence();
+                    named_barrier_sync(1 + e, 128);
+                    if (leader) atomicAdd(sig.done + tt / sig.chunk_tts, 1u);
+                }
+            }
         }
         if (leader && y_tma) bulk_wait_group0();
     }
@@ -418,6 +444,11 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
+    // A CTA that gave up raises every chunk to its maximum, so that nothing waiting
+    // on a count is left waiting (the status word carries the error).
+    if (threadIdx.x == 0 && sig.done != nullptr && *abort_flag) {
+        for (int i = 0; i < sig.nchunks; ++i) atomicMax(sig.done + i, 0x7FFFFFFFu);
+    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -428,7 +459,7 @@ constexpr size_t kMaxSmem = kQmvMaxSmem;
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const void* bias, void* y, cudaStream_t st,
-                        const char** msg) {
+                        const char** msg, const TcSignal& sig, int grid_cap) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     auto enc = tensor_map_encoder();
     if (!enc) {
@@ -494,52 +525,61 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
         configured[dev] = true;
     }
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
-    const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+    const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
+    const int grid = (int)(tiles < cap ? tiles : cap);
     qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), static_cast<const uint16_t*>(bias),
-        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k, y_tma ? 1 : 0);
+        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k, y_tma ? 1 : 0, sig);
     return cudaGetLastError();
+}
+
+// Tokens per tile for an M x N problem; 0 stands for the 16-token tile with X resident.
+// Up to 128 tokens: the smallest of 16 / 64 / 128 that covers M, so short activations do
+// not pay for empty MMA columns.  Beyond that the tile height is chosen so the tiles fill
+// whole waves of the SMs: cost = waves x (per-step time + a fixed per-tile share), the
+// step time being the MMA's (BT tokens) or the unpacking's (about 128 tokens' worth for
+// W4, 288 for W8), whichever is longer.  1024 x 3072 output at W4 thus runs as 144 tiles
+// of 176 tokens in one wave instead of 96 tiles of 256.
+template <int BITS>
+int choose_tile(int64_t m, int64_t k, int64_t n, int grid_cap) {
+    constexpr int SWs = BITS == 4 ? 16 : 12;
+    using CR = TcCfg<BITS, 16, 1, SWs, 14, true>;
+    if (m <= 16) return smem_bytes<CR, true, 16>(k) <= kMaxSmem ? 0 : 16;
+    if (m <= 64) return 64;
+    if (m <= 128) return 128;
+    const int64_t sms = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
+    const int64_t nft = (n + 127) / 128;
+    const int64_t dq = BITS == 4 ? 128 : 288, fixed = 32;
+    int64_t best = -1;
+    int bt = 128;
+    for (int cand : {128, 176, 240, 256}) {
+        const int64_t tiles = (m + cand - 1) / cand * nft;
+        const int64_t cost = (tiles + sms - 1) / sms * ((cand > dq ? cand : dq) + fixed);
+        if (best < 0 || cost <= best) {                // ties go to the taller tile
+            best = cost;
+            bt = cand;
+        }
+    }
+    return bt;
 }
 
 template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                            const void* scales, const void* biases, int64_t n, const void* bias,
-                           void* y, cudaStream_t st, const char** msg) {
-    // Tokens per tile.  Up to 128 tokens: the smallest of 16 / 64 / 128 that covers
-    // M, so short activations do not pay for empty MMA columns.  Beyond that the
-    // tile height is chosen so the tiles fill whole waves of the SMs: cost = waves x
-    // (per-step time + a fixed per-tile share), the step time being the MMA's (BT
-    // tokens) or the unpacking's (about 128 tokens' worth for W4, 288 for W8),
-    // whichever is longer.  1024 x 3072 output at W4 thus runs as 144 tiles of 176
-    // tokens in one wave instead of 96 tiles of 256.  Ring depths fill the shared
-    // memory budget; the packed-weight ring is the deep one.
+                           void* y, cudaStream_t st, const char** msg, const TcSignal& sig,
+                           int grid_cap) {
+    // Ring depths fill the shared memory budget; the packed-weight ring is the deep one.
     constexpr int SWs = BITS == 4 ? 16 : 12;
-    using CR = TcCfg<BITS, 16, 1, SWs, 14, true>;
-    if (m <= 16 && smem_bytes<CR, true, 16>(k) <= kMaxSmem)
-        return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    if (m <= 16) return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-    if (m <= 64) return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
     constexpr int SWL = BITS == 4 ? 8 : 4;
-    int bt = 128;
-    if (m > 128) {
-        const int64_t sms = num_sms(), nft = (n + 127) / 128;
-        const int64_t dq = BITS == 4 ? 128 : 288, fixed = 32;
-        int64_t best = -1;
-        for (int cand : {128, 176, 240, 256}) {
-            const int64_t tiles = (m + cand - 1) / cand * nft;
-            const int64_t cost = (tiles + sms - 1) / sms * ((cand > dq ? cand : dq) + fixed);
-            if (best < 0 || cost <= best) {                // ties go to the taller tile
-                best = cost;
-                bt = cand;
-            }
-        }
-    }
-    switch (bt) {
-        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    switch (choose_tile<BITS>(m, k, n, grid_cap)) {
+        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
     }
 }
 
@@ -561,8 +601,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,
                           const void* bias, void* y, cudaStream_t st, const char** msg) {
-    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg)
-                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+    const TcSignal off{nullptr, 1, 0};
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg, off, 0)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg, off, 0);
+}
+
+int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) {
+    const int t = bits == 4 ? choose_tile<4>(m, k, n, grid_cap) : choose_tile<8>(m, k, n, grid_cap);
+    return t == 0 ? 16 : t;
+}
+
+cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
+                                 const void* scales, const void* biases, int64_t n, int bits,
+                                 const void* bias, void* y, cudaStream_t st, const char** msg,
+                                 uint32_t* done, int chunk_tts, int nchunks, int grid_cap) {
+    const TcSignal sig{done, chunk_tts, nchunks};
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
 }
 
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st) {

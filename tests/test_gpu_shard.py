@@ -94,7 +94,7 @@ def _rank_main(rank, world, port, m, k, n, bits, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("m", [4, 256])
+@pytest.mark.parametrize("m", [4, 256, 1000])
 def test_two_gpu_sharded_linear_reassembles_the_full_product(bits, m):
     import torch.multiprocessing as mp
     world, k, n = 2, 512, 1024
