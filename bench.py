@@ -58,13 +58,16 @@ def algorithmic(m, k, n, bits, world=1):
     return flops, byts
 
 
-def peaks():
+def peaks(sustained=False):
+    """(HBM GB/s, bf16 TFLOP/s, source).  The burst bf16 figure suits a kernel timed alone; a
+    step of tens of milliseconds runs under the power cap and is held to the sustained one."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+        tc = p.get("bf16_tflops_sustained", p["bf16_tflops"]) if sustained else p["bf16_tflops"]
+        return p["hbm_gbs"], tc, "measured"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1400.0 if sustained else 1590.0, "fallback"
 
 
 def traffic_from_profiles(workload):
@@ -260,7 +263,7 @@ def run_flux(args, rank, world, local):
     e2e_ms = timed(e2e_step, max(2, args.steps // 2))
 
     value = total_flops * world / (lin_ms * 1e-3) / 1e12
-    hbm, tc, src = peaks()
+    hbm, tc, src = peaks(sustained=True)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cv, threads, sample = cpu_reference(argparse.Namespace(steps=3, warmup=3), "cfg4")
@@ -284,7 +287,7 @@ def run_flux(args, rank, world, local):
                        "parallelism": "single GPU" if world == 1 else f"{world} replicas",
                        "l2": "weights (8.5 GB) exceed L2; 256 MiB write before every step anyway"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc, "unit": "TFLOP/s",
-                         "frac": achieved / tc, "peak_source": f"{src} burst bf16 (MEASURED_PEAKS.json)",
+                         "frac": achieved / tc, "peak_source": f"{src} sustained bf16 (MEASURED_PEAKS.json)",
                          "traffic": None, "kernel_ms": lin_ms},
             "cpu_baseline": cpu,
             "e2e": {"value": total_flops * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
