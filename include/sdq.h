@@ -94,16 +94,54 @@ int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases,
  * (mlx.rs:386-397) as called by QuantizedArray::matmul (mlx.rs:1952-1975) and,
  * with `bias`, the separate `y.add(bias)` of quantized::linear
  * (crates/sd-models/src/mlx/quantized.rs:314-317).  `transpose` must be true
- * (the reference always passes true).  m >= 1.  Every shape runs the tcgen05
- * tensor-core kernel; the token tile (16 / 64 / 128 / 256 rows of x) follows
- * m, and for m <= 16 the activations stay resident in shared memory while the
- * packed weight streams from HBM.  x and wq must be 16-byte aligned.
+ * (the reference always passes true).  m >= 1.  For m <= 8 a weight-stream
+ * kernel (TMA ring of packed words, mma.sync on the raw codes, HBM-bound)
+ * runs when k * bits / 8 is a multiple of 128; every other shape runs the
+ * tcgen05 tensor-core kernel, whose token tile (16 .. 256 rows of x) follows
+ * m and the SM count, and for m <= 16 keeps the activations resident in
+ * shared memory while the packed weight streams from HBM.  x and wq must be
+ * 16-byte aligned.
  */
 int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                          const uint32_t* wq, const void* scales, const void* biases,
                          sdq_dtype sb_dtype, int64_t n, int transpose, int group_size, int bits,
                          const char* mode, const void* bias, void* y, sdq_dtype y_dtype,
                          void* stream);
+
+/* Activations for sdq_quantized_matmul_epilogue (values fixed; part of the ABI). */
+#define SDQ_ACT_NONE 0
+#define SDQ_ACT_GELU_TANH 1 /* 0.5 a (1 + tanh(sqrt(2/pi) (a + 0.044715 a^3))), mlx.rs:1033-1052 */
+#define SDQ_ACT_SILU 2      /* a * sigmoid(a), mlx.rs:697-705 */
+
+/*
+ * The quantised linear with its elementwise consumers fused into the output
+ * stage:
+ *
+ *   y[t,f] = residual[t,f] + gate[f] * act(x[t,:] . dequant(w)[f,:] + bias[f])
+ *
+ * computed in f32 from the accumulator and rounded to bf16 once.  Every term
+ * is optional: bias, gate and residual may be NULL (then 0, 1 and 0), act is
+ * one of SDQ_ACT_*.  No single reference function does this; it replaces the
+ * chains the reference's Flux model builds around a linear, each op a
+ * separate pass over [m, n]:
+ *   x.add(linear(a).mul(gate))   crates/sd-models/src/mlx/flux.rs:389-398,
+ *                                408-414 and 470 (residual + gate, "m[2]" /
+ *                                "m[5]" of the block's modulation)
+ *   linear(a).gelu_approx()      flux.rs:400-407 (the MLP's first layer)
+ *   linear(a).silu()             flux.rs:491-495 (the conditioning MLPs)
+ * with the linear being quantized::linear (quantized.rs:298-318).
+ * gate and bias are [n] bf16, residual [m, n] bf16 (row-major, contiguous).
+ * residual may be y itself (in-place update of a residual stream) but must
+ * not otherwise overlap y.  The other arguments and the dispatch (small-M
+ * weight stream for m <= 8, tensor cores otherwise) are those of
+ * sdq_quantized_matmul with transpose = 1 and mode "affine".
+ */
+int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                                  const uint32_t* wq, const void* scales, const void* biases,
+                                  sdq_dtype sb_dtype, int64_t n, int group_size, int bits,
+                                  const void* bias, int act, const void* gate,
+                                  const void* residual, void* y, sdq_dtype y_dtype,
+                                  void* stream);
 
 /*
  * Bytes a quantised [n,k] weight occupies, packed words plus scales and

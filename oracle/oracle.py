@@ -130,6 +130,36 @@ def qmatmul(x_bf16: np.ndarray, wq, s, b, n: int, bits: int, bias_bf16=None, thr
     return y
 
 
+ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
+
+
+def epilogue(acc: np.ndarray, bias_bf16=None, act: int = ACT_NONE, gate_bf16=None, resid_bf16=None):
+    """The chains the reference's Flux model builds around a linear, in f64:
+    ``resid + gate * act(acc + bias)``.
+
+    * bias: quantized::linear's ``y.add(bias)`` (crates/sd-models/src/mlx/quantized.rs:314-317);
+    * act: ``gelu_approx`` = 0.5 a (1 + tanh(sqrt(2/pi) (a + 0.044715 a^3)))
+      (crates/sd-tensor/src/mlx.rs:1033-1052) after the MLP's first layer (flux.rs:400-407), or
+      ``silu`` = a * sigmoid(a) (mlx.rs:697-705) inside the conditioning MLPs (flux.rs:491-495);
+    * gate and resid: ``x.add(&linear(a).mul(&m[2]))`` (flux.rs:389-398, 408-414, 470).
+    bias and gate are [n] bf16 bit patterns, resid [m, n]; returns f64 [m, n]."""
+    a = acc.astype(np.float64)
+    if bias_bf16 is not None:
+        a = a + bf16_bits_to_f32(np.asarray(bias_bf16)).astype(np.float64)[None, :]
+    if act == ACT_GELU_TANH:
+        c = np.sqrt(2.0 / np.pi)
+        a = 0.5 * a * (1.0 + np.tanh(c * (a + 0.044715 * a ** 3)))
+    elif act == ACT_SILU:
+        a = a / (1.0 + np.exp(-a))
+    elif act != ACT_NONE:
+        raise ValueError(f"oracle.epilogue: unknown activation {act}")
+    if gate_bf16 is not None:
+        a = a * bf16_bits_to_f32(np.asarray(gate_bf16)).astype(np.float64)[None, :]
+    if resid_bf16 is not None:
+        a = a + bf16_bits_to_f32(np.asarray(resid_bf16)).astype(np.float64)
+    return a
+
+
 def resident_bytes(n: int, k: int, bits: int, group_size: int = GROUP) -> int:
     return int(lib().oracle_resident_bytes(n, k, group_size, bits))
 

@@ -139,6 +139,26 @@ int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const u
         return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
     return check_device();
 }
+
+// The dispatch shared by the matmul entry points: the small-M weight stream where it
+// serves the shape, the tensor-core kernel otherwise.
+int run_qmm(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
+            const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y, void* stream,
+            const char* fn) {
+    const char* msg = nullptr;
+    bool taken = false;
+    cudaError_t e = launch_qmv(x, m, k, wq, scales, biases, n, bits, epi, y,
+                               static_cast<cudaStream_t>(stream), &msg, &taken);
+    if (e == cudaSuccess && !taken)
+        e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, epi, y,
+                          static_cast<cudaStream_t>(stream), &msg);
+    if (e != cudaSuccess) {
+        if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
+        return fail(SDQ_ERR_CUDA, "%s: kernel launch: %s (%s)", fn, cudaGetErrorString(e),
+                    cudaGetErrorName(e));
+    }
+    return ok();
+}
 }  // namespace sdq
 
 extern "C" {
@@ -212,18 +232,36 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
     if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, transpose,
                                 group_size, bits, mode, bias, y, y_dtype, fn)))
         return rc;
-    const char* msg = nullptr;
-    bool taken = false;
-    cudaError_t e = launch_qmv(x, m, k, wq, scales, biases, n, bits, bias, y,
-                               static_cast<cudaStream_t>(stream), &msg, &taken);
-    if (e == cudaSuccess && !taken)
-        e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, bias, y,
-                          static_cast<cudaStream_t>(stream), &msg);
-    if (e != cudaSuccess) {
-        if (msg) return fail(SDQ_ERR_CUDA, "%s: %s", fn, msg);
-        return cuda_fail("sdq_quantized_matmul: tensor-core kernel", e);
+    return run_qmm(x, m, k, wq, scales, biases, n, bits, bias_only(bias), y, stream, fn);
+}
+
+int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
+                                  const uint32_t* wq, const void* scales, const void* biases,
+                                  sdq_dtype sb_dtype, int64_t n, int group_size, int bits,
+                                  const void* bias, int act, const void* gate,
+                                  const void* residual, void* y, sdq_dtype y_dtype,
+                                  void* stream) {
+    const char* fn = "sdq_quantized_matmul_epilogue";
+    int rc;
+    if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, 1, group_size,
+                                bits, "affine", bias, y, y_dtype, fn)))
+        return rc;
+    if (act != SDQ_ACT_NONE && act != SDQ_ACT_GELU_TANH && act != SDQ_ACT_SILU)
+        return fail(SDQ_ERR_INVALID, "%s: act must be SDQ_ACT_NONE, _GELU_TANH or _SILU; got %d", fn, act);
+    if ((gate && !aligned(gate, 2)) || (residual && !aligned(residual, 2)))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned gate or residual (bf16 needs 2 bytes)", fn);
+    if (residual && residual != y) {
+        // Partial overlap would let one tile read what another already wrote.
+        const uintptr_t r0 = reinterpret_cast<uintptr_t>(residual), y0 = reinterpret_cast<uintptr_t>(y);
+        const uintptr_t bytes = static_cast<uintptr_t>(m) * static_cast<uintptr_t>(n) * 2;
+        if (r0 < y0 + bytes && y0 < r0 + bytes)
+            return fail(SDQ_ERR_INVALID, "%s: residual overlaps y without being y", fn);
     }
-    return ok();
+    EpiArgs epi = bias_only(bias);
+    epi.act = act;
+    epi.gate = static_cast<const uint16_t*>(gate);
+    epi.resid = static_cast<const uint16_t*>(residual);
+    return run_qmm(x, m, k, wq, scales, biases, n, bits, epi, y, stream, fn);
 }
 
 int sdq_device_status(void* stream) {

@@ -20,6 +20,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // Opt-in dynamic shared memory per block on sm_100 (227 KB).
 constexpr size_t kQmvMaxSmem = 232448;
 
+// The output stage of the matmul kernels: y = resid + gate[f] * act(acc + bias[f]),
+// computed in f32 and rounded to bf16 once.  Null pointers drop their term; act is one
+// of SDQ_ACT_*.  resid is [M, N] and may be y itself.
+struct EpiArgs {
+    const uint16_t* bias = nullptr;
+    const uint16_t* gate = nullptr;
+    const uint16_t* resid = nullptr;
+    int act = SDQ_ACT_NONE;
+    // Whether anything beyond the bias is asked for.
+    bool fused() const { return gate != nullptr || resid != nullptr || act != SDQ_ACT_NONE; }
+};
+inline EpiArgs bias_only(const void* bias) {
+    EpiArgs e;
+    e.bias = static_cast<const uint16_t*>(bias);
+    return e;
+}
+
 cudaError_t launch_quantize(const void* w, bool w_bf16, int64_t n, int64_t k, int bits,
                             uint32_t* wq, void* scales, void* biases, cudaStream_t st);
 cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases,
@@ -30,7 +47,7 @@ cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void
 // or cudaSuccess; `msg` receives a description when tensor-map encoding fails.
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,
-                          const void* bias, void* y, cudaStream_t st, const char** msg);
+                          const EpiArgs& epi, void* y, cudaStream_t st, const char** msg);
 
 // The argument and device checks of sdq_quantized_matmul (status, message set on failure).
 int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
@@ -45,14 +62,14 @@ int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const u
 int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap);
 cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                                  const void* scales, const void* biases, int64_t n, int bits,
-                                 const void* bias, void* y, cudaStream_t st, const char** msg,
+                                 const EpiArgs& epi, void* y, cudaStream_t st, const char** msg,
                                  uint32_t* done, int chunk_tts, int nchunks, int grid_cap);
 
 // Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs).
 // Sets *taken = false, launching nothing, for shapes it does not serve (M > 8, or X too
 // large to stay resident beside the weight ring); the caller then uses launch_qmm_tc.
 cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                       const void* biases, int64_t n, int bits, const void* bias, void* y,
+                       const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y,
                        cudaStream_t st, const char** msg, bool* taken);
 
 // Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.

@@ -34,8 +34,10 @@
 //               (TMEM lane r), so the groups store, into different A slots, the
 //               same TMEM lanes
 //   last 4      epilogue: 32-token chunks of the accumulator -> registers
-//               (+bias, packed to bf16) -> shared staging -> TMA tensor store,
-//               with the accumulator released as soon as it has been read
+//               (+bias, or the fused stage resid + gate * act(acc + bias) with
+//               the residual tile copied in by TMA ahead of the accumulator;
+//               packed to bf16) -> shared staging -> TMA tensor store, with the
+//               accumulator released as soon as it has been read
 // A packed-weight slot is released only after the words read from it have been
 // consumed (stored to TMEM): releasing it right after the shared-memory reads let
 // the slot's next TMA fill land before those reads returned, which showed up as
@@ -50,6 +52,7 @@
 #include <cudaTypedefs.h>
 
 #include "sdq_dequant.cuh"
+#include "sdq_epilogue.cuh"
 #include "sdq_internal.h"
 #include "sdq_ptx.cuh"
 
@@ -112,10 +115,11 @@ size_t smem_bytes(int64_t k) {
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 __global__ void __launch_bounds__(tc_threads(BITS), 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                  const __grid_constant__ CUtensorMap tmY,
+                  const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
-                  const uint16_t* __restrict__ biases, const uint16_t* __restrict__ bias,
-                  uint16_t* __restrict__ y, int M, int N, int K, int y_tma, const TcSignal sig) {
+                  const uint16_t* __restrict__ biases, const EpiArgs epi,
+                  uint16_t* y, int M, int N, int K, int y_tma, int r_tma,
+                  const TcSignal sig) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -143,7 +147,8 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
     uint64_t* dempty = dfull + 1;            // accumulator drained        count 128 per epilogue group
     uint64_t* drain = dfull + 2;             // abort drain of the MMA pipe
     uint64_t* xfull = dfull + 3;             // resident X landed          count 1 + tx
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 1);
+    uint64_t* rfull = dfull + 4;             // residual tile landed in the staging  count 1 + tx
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     unsigned int* status = &g_tc_status;
 
@@ -157,11 +162,13 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         mbar_init(dempty, 128 * kEpiGroups);
         mbar_init(drain, 1);
         mbar_init(xfull, 1);
+        mbar_init(rfull, 1);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
         if (y_tma) tma_prefetch_desc(&tmY);
+        if (r_tma) tma_prefetch_desc(&tmR);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -369,17 +376,40 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         const int fl = 32 * (warp & 3) + lane;            // feature row within the tile
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         const bool leader = (warp & 3) == 0 && lane == 0;
+        // Beyond the bias, the fused stage y = resid + gate * act(acc + bias).  With a
+        // TMA-able residual, its tile is copied into the staging chunks before the
+        // accumulator is waited on (the copy overlaps the tile's main loop) and the output
+        // is formed in place there; otherwise each thread loads its residual elements.
+        static_assert(kEpiGroups == 1, "one residual barrier serves one epilogue group");
+        const bool fused = epi.gate != nullptr || epi.resid != nullptr || epi.act != SDQ_ACT_NONE;
         int tc = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
             const int tt = tile / nft, ft = tile - tt * nft;
             const int f = ft * C::BF + fl;
-            const float badd = (bias != nullptr && f < N) ? bf16_bits_to_f32(bias[f]) : 0.f;
+            const float badd = (epi.bias != nullptr && f < N) ? bf16_bits_to_f32(epi.bias[f]) : 0.f;
+            const float gmul = (epi.gate != nullptr && f < N) ? bf16_bits_to_f32(epi.gate[f]) : 1.f;
             // The staging chunks of this group must have been read by the previous
             // tile's stores before they are overwritten.
             if (leader && y_tma) bulk_wait_group_read0();
             named_barrier_sync(1 + e, 128);
-            const bool ok = __all_sync(0xffffffffu,
-                                       mbar_wait_sleep(dfull, tc & 1, abort_flag, status, 8u, 64));
+            bool ok = true;
+            if (r_tma) {
+                if (leader) {
+                    uint32_t bytes = 0;
+                    for (int c = e; c < NCH; c += kEpiGroups)
+                        if (tt * BT + c * CW < M) bytes += CW * C::BF * 2;
+                    mbar_arrive_expect_tx(rfull, bytes);
+                    for (int c = e; c < NCH; c += kEpiGroups)
+                        if (tt * BT + c * CW < M)
+                            tma_load_2d(sY + (size_t)c * CW * C::BF * 2, &tmR, rfull, ft * C::BF,
+                                        tt * BT + c * CW);
+                }
+                ok = __all_sync(0xffffffffu, mbar_wait_sleep(rfull, tc & 1, abort_flag, status, 8u, 64));
+                // A copy still in flight must land before shared memory is given up.
+                if (!ok && leader) mbar_wait_drain(rfull, tc & 1);
+            }
+            ok = ok && __all_sync(0xffffffffu,
+                                  mbar_wait_sleep(dfull, tc & 1, abort_flag, status, 8u, 64));
             if (ok) {
                 tc_fence_after();
                 for (int c = e; c < NCH; c += kEpiGroups) {
@@ -390,10 +420,25 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                         __syncwarp();
                         tmem_ld16(tmem + lane_base + C::D_COL + (uint32_t)(CW * c + 16 * h), v);
                         tc_wait_ld();
+                        if (!fused) {
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            yrow[(16 * h + j) * C::BF] =
-                                (uint16_t)(pack_bf16x2(__uint_as_float(v[j]) + badd, 0.f) & 0xFFFFu);
+                            for (int j = 0; j < 16; ++j)
+                                yrow[(16 * h + j) * C::BF] =
+                                    (uint16_t)(pack_bf16x2(__uint_as_float(v[j]) + badd, 0.f) & 0xFFFFu);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const int r = 16 * h + j;
+                                float a = epi_activation(__uint_as_float(v[j]) + badd, epi.act) * gmul;
+                                if (r_tma) {
+                                    a += bf16_bits_to_f32(yrow[r * C::BF]);
+                                } else if (epi.resid != nullptr) {
+                                    const int t = tt * BT + c * CW + r;
+                                    if (t < M && f < N) a += bf16_bits_to_f32(epi.resid[(size_t)t * N + f]);
+                                }
+                                yrow[r * C::BF] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
+                            }
+                        }
                     }
                 }
                 __syncwarp();
@@ -458,7 +503,7 @@ constexpr size_t kMaxSmem = kQmvMaxSmem;
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                        const void* biases, int64_t n, const void* bias, void* y, cudaStream_t st,
+                        const void* biases, int64_t n, const EpiArgs& epi, void* y, cudaStream_t st,
                         const char** msg, const TcSignal& sig, int grid_cap) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     auto enc = tensor_map_encoder();
@@ -513,6 +558,24 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
             return cudaErrorInvalidValue;
         }
     }
+    // The residual, same geometry as Y, is copied in by TMA under the same conditions.
+    CUtensorMap tmR;
+    std::memset(&tmR, 0, sizeof(tmR));
+    const bool r_tma = y_tma && epi.resid != nullptr && (reinterpret_cast<uintptr_t>(epi.resid) % 16) == 0;
+    if (r_tma) {
+        cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+        cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+        cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)C::CW};
+        cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&tmR, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(epi.resid),
+                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            *msg = "cuTensorMapEncodeTiled rejected the residual tensor map";
+            return cudaErrorInvalidValue;
+        }
+    }
     const size_t smem = smem_bytes<C, XRES, BT>(k);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -528,9 +591,9 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
     const int grid = (int)(tiles < cap ? tiles : cap);
     qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, tc_threads(BITS), smem, st>>>(
-        tmX, tmW, tmY, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
-        static_cast<const uint16_t*>(biases), static_cast<const uint16_t*>(bias),
-        static_cast<uint16_t*>(y), (int)m, (int)n, (int)k, y_tma ? 1 : 0, sig);
+        tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
+        static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
+        y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
     return cudaGetLastError();
 }
 
@@ -566,20 +629,20 @@ int choose_tile(int64_t m, int64_t k, int64_t n, int grid_cap) {
 
 template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
-                           const void* scales, const void* biases, int64_t n, const void* bias,
+                           const void* scales, const void* biases, int64_t n, const EpiArgs& epi,
                            void* y, cudaStream_t st, const char** msg, const TcSignal& sig,
                            int grid_cap) {
     // Ring depths fill the shared memory budget; the packed-weight ring is the deep one.
     constexpr int SWs = BITS == 4 ? 16 : 12;
     constexpr int SWL = BITS == 4 ? 8 : 4;
     switch (choose_tile<BITS>(m, k, n, grid_cap)) {
-        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
-        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
     }
 }
 
@@ -600,10 +663,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,
-                          const void* bias, void* y, cudaStream_t st, const char** msg) {
+                          const EpiArgs& epi, void* y, cudaStream_t st, const char** msg) {
     const TcSignal off{nullptr, 1, 0};
-    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg, off, 0)
-                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg, off, 0);
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, off, 0)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, off, 0);
 }
 
 int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) {
@@ -613,11 +676,11 @@ int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) 
 
 cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                                  const void* scales, const void* biases, int64_t n, int bits,
-                                 const void* bias, void* y, cudaStream_t st, const char** msg,
+                                 const EpiArgs& epi, void* y, cudaStream_t st, const char** msg,
                                  uint32_t* done, int chunk_tts, int nchunks, int grid_cap) {
     const TcSignal sig{done, chunk_tts, nchunks};
-    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap)
-                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg, sig, grid_cap);
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
 }
 
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st) {

@@ -54,6 +54,7 @@
 #include <cudaTypedefs.h>
 
 #include "sdq_dequant.cuh"
+#include "sdq_epilogue.cuh"
 #include "sdq_internal.h"
 #include "sdq_ptx.cuh"
 
@@ -135,7 +136,7 @@ template <int BITS, int TR>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_kernel(const __grid_constant__ CUtensorMap tmW, const uint16_t* __restrict__ x,
                const uint16_t* __restrict__ scales, const uint16_t* __restrict__ biases,
-               const uint16_t* __restrict__ bias, uint16_t* __restrict__ y, int M, int N, int K) {
+               const EpiArgs epi, uint16_t* y, int M, int N, int K) {
     using C = QmvCfg<BITS, TR>;
     constexpr int SW = C::SW;
     extern __shared__ uint8_t smem_raw[];
@@ -365,13 +366,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float4 v = rb[((p - 1) * C::RS + c) * 32 + lane];
                     acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
                 }
-                const float add0 = (bias != nullptr && r0 < N) ? bf16_bits_to_f32(bias[r0]) : 0.f;
-                const float add1 = (bias != nullptr && r1 < N) ? bf16_bits_to_f32(bias[r1]) : 0.f;
+                // y = resid + gate * act(acc + bias), rounded once (null terms drop out).
                 const int m0i = 2 * t, m1i = 2 * t + 1;
-                if (r0 < N && m0i < M) y[(int64_t)m0i * N + r0] = (uint16_t)(pack_bf16x2(acc[0] + add0, 0.f) & 0xFFFFu);
-                if (r0 < N && m1i < M) y[(int64_t)m1i * N + r0] = (uint16_t)(pack_bf16x2(acc[1] + add0, 0.f) & 0xFFFFu);
-                if (r1 < N && m0i < M) y[(int64_t)m0i * N + r1] = (uint16_t)(pack_bf16x2(acc[2] + add1, 0.f) & 0xFFFFu);
-                if (r1 < N && m1i < M) y[(int64_t)m1i * N + r1] = (uint16_t)(pack_bf16x2(acc[3] + add1, 0.f) & 0xFFFFu);
+                auto put = [&](float a, int tok, int row) {
+                    if (row >= N || tok >= M) return;
+                    const int64_t o = (int64_t)tok * N + row;
+                    a += epi.bias != nullptr ? bf16_bits_to_f32(epi.bias[row]) : 0.f;
+                    a = epi_activation(a, epi.act);
+                    if (epi.gate != nullptr) a *= bf16_bits_to_f32(epi.gate[row]);
+                    if (epi.resid != nullptr) a += bf16_bits_to_f32(epi.resid[o]);
+                    y[o] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
+                };
+                put(acc[0], m0i, r0);
+                put(acc[1], m1i, r0);
+                put(acc[2], m0i, r1);
+                put(acc[3], m1i, r1);
             }
             tile_stage0 += stages_per_tile;
         }
@@ -381,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BITS, int TR>
 cudaError_t launch_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                     const void* biases, int64_t n, const void* bias, void* y,
+                     const void* biases, int64_t n, const EpiArgs& epi, void* y,
                      cudaStream_t st, const char** msg) {
     using C = QmvCfg<BITS, TR>;
     auto enc = tensor_map_encoder();
@@ -419,7 +428,7 @@ cudaError_t launch_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, co
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
     qmv_kernel<BITS, TR><<<grid, kThreads, smem, st>>>(
         tmW, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
-        static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
+        epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
     return cudaGetLastError();
 }
 
@@ -448,7 +457,7 @@ int pick_rows(int64_t n) {
 
 template <int BITS>
 cudaError_t launch_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                        const void* biases, int64_t n, const void* bias, void* y, cudaStream_t st,
+                        const void* biases, int64_t n, const EpiArgs& epi, void* y, cudaStream_t st,
                         const char** msg, bool* taken) {
     // A stage is 128 bytes of every row: K must be a whole number of stages; a
     // stage's scales of one row are copied as one 8-byte (W4) / 4-byte (W8) piece.
@@ -467,22 +476,22 @@ cudaError_t launch_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     }
     *taken = true;
     switch (tr) {
-        case 128: return launch_t<BITS, 128>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        case 64: return launch_t<BITS, 64>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        case 32: return launch_t<BITS, 32>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
-        default: return launch_t<BITS, 16>(x, m, k, wq, scales, biases, n, bias, y, st, msg);
+        case 128: return launch_t<BITS, 128>(x, m, k, wq, scales, biases, n, epi, y, st, msg);
+        case 64: return launch_t<BITS, 64>(x, m, k, wq, scales, biases, n, epi, y, st, msg);
+        case 32: return launch_t<BITS, 32>(x, m, k, wq, scales, biases, n, epi, y, st, msg);
+        default: return launch_t<BITS, 16>(x, m, k, wq, scales, biases, n, epi, y, st, msg);
     }
 }
 
 }  // namespace
 
 cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                       const void* biases, int64_t n, int bits, const void* bias, void* y,
+                       const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y,
                        cudaStream_t st, const char** msg, bool* taken) {
     *taken = false;
     if (m < 1 || m > 8) return cudaSuccess;
-    return bits == 4 ? launch_bits<4>(x, m, k, wq, scales, biases, n, bias, y, st, msg, taken)
-                     : launch_bits<8>(x, m, k, wq, scales, biases, n, bias, y, st, msg, taken);
+    return bits == 4 ? launch_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken)
+                     : launch_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken);
 }
 
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st) {

@@ -252,7 +252,8 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->ev_start, 0);
     if (e != cudaSuccess) return cuda_err("stream set-up", e);
     const char* msg = nullptr;
-    e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits, bias_local, mine, st,
+    e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits,
+                                  sdq::bias_only(bias_local), mine, st,
                                   &msg, c->counters, (int)tpc, (int)nch, 0);
     if (e != cudaSuccess) {
         if (msg) {

@@ -19,7 +19,8 @@ from ._abi import (SDQ_BF16, SDQ_ERR_CUDA, SDQ_ERR_INVALID, SDQ_ERR_NCCL, SDQ_ER
                    SDQ_ERR_UNSUPPORTED, SDQ_F16, SDQ_F32, SDQ_OK, SdqError, check, last_error, lib)
 
 __all__ = [
-    "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "resident_bytes",
+    "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "quantized_matmul_epilogue",
+    "resident_bytes", "ACT_NONE", "ACT_GELU_TANH", "ACT_SILU",
     "device_status", "Comm", "quantized_matmul_sharded", "shard_rows", "unshard", "GROUP_SIZE", "MODE",
     "SDQ_OK", "SDQ_ERR_INVALID", "SDQ_ERR_UNSUPPORTED", "SDQ_ERR_CUDA", "SDQ_ERR_TIMEOUT",
     "SDQ_ERR_NCCL",
@@ -29,6 +30,11 @@ __all__ = [
 GROUP_SIZE = 64
 #: The quantisation mode the reference always asks for (mlx.rs:1830-1832).
 MODE = "affine"
+
+#: Activations of the fused output stage (include/sdq.h SDQ_ACT_*).
+ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
+_ACTS = {None: ACT_NONE, "none": ACT_NONE, "gelu_approx": ACT_GELU_TANH, "gelu_tanh": ACT_GELU_TANH,
+         "silu": ACT_SILU, ACT_NONE: ACT_NONE, ACT_GELU_TANH: ACT_GELU_TANH, ACT_SILU: ACT_SILU}
 
 _DT = {torch.float32: SDQ_F32, torch.bfloat16: SDQ_BF16, torch.float16: SDQ_F16}
 
@@ -110,6 +116,39 @@ def quantized_matmul(x: torch.Tensor, wq, scales, biases, group_size: int = GROU
     return out
 
 
+def quantized_matmul_epilogue(x: torch.Tensor, wq, scales, biases, group_size: int = GROUP_SIZE,
+                              bits: int = 4, bias: torch.Tensor | None = None, act=None,
+                              gate: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                              out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """``residual + gate * act(x . dequant(w)^T + bias)`` in one kernel, rounded to bf16 once.
+
+    Replaces the reference's ``x.add(&linear(a).mul(gate))`` and ``linear(a).gelu_approx()`` /
+    ``.silu()`` chains (crates/sd-models/src/mlx/flux.rs:389-414, 470, 491-495).  ``act`` is
+    None, ``"gelu_approx"`` or ``"silu"`` (or an ``ACT_*`` value); ``gate`` and ``bias`` hold
+    ``n`` values (any leading 1-sized dims, as a modulation vector has), ``residual`` has the
+    output's shape.  ``out`` may be ``residual`` itself (an in-place residual update)."""
+    if act not in _ACTS:
+        raise SdqError(SDQ_ERR_INVALID, f"unknown activation {act!r}")
+    _need_cuda(x, wq, scales, biases, bias, gate, residual, out)
+    lead = x.shape[:-1]
+    k = x.shape[-1]
+    m = 1
+    for d in lead:
+        m *= d
+    n = wq.shape[0]
+    for name, t in (("bias", bias), ("gate", gate)):
+        if t is not None and t.numel() != n:
+            raise SdqError(SDQ_ERR_INVALID, f"{name} holds {t.numel()} values, the layer has {n} outputs")
+    if residual is not None and residual.numel() != m * n:
+        raise SdqError(SDQ_ERR_INVALID, f"residual of shape {tuple(residual.shape)} is not [{m}, {n}]")
+    if out is None:
+        out = torch.empty((*lead, n), device=x.device, dtype=torch.bfloat16)
+    check(lib().sdq_quantized_matmul_epilogue(
+        _ptr(x), _dt(x), m, k, _ptr(wq), _ptr(scales), _ptr(biases), _dt(scales), n, group_size, bits,
+        _ptr(bias), _ACTS[act], _ptr(gate), _ptr(residual), _ptr(out), _dt(out), _stream(stream)))
+    return out
+
+
 def resident_bytes(n: int, k: int, bits: int, group_size: int = GROUP_SIZE, sb_bytes: int = 4) -> int:
     """Packed words plus scales and biases; ``sb_bytes=4`` counts them as the reference does
     (mlx.rs:1981-1985), ``sb_bytes=2`` is what this library actually stores."""
@@ -151,6 +190,14 @@ class QuantizedArray:
         given, receives the result."""
         return quantized_matmul(x, self.weight, self.scales, self.biases, self.group_size, self.bits,
                                 bias=bias, out=out, stream=stream)
+
+    def matmul_fused(self, x: torch.Tensor, bias=None, act=None, gate=None, residual=None,
+                     out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """``residual + gate * act(x @ weight.T + bias)`` in one kernel (see
+        :func:`quantized_matmul_epilogue`)."""
+        return quantized_matmul_epilogue(x, self.weight, self.scales, self.biases, self.group_size,
+                                         self.bits, bias=bias, act=act, gate=gate, residual=residual,
+                                         out=out, stream=stream)
 
     def resident_bytes(self) -> int:
         """Bytes this weight occupies, counted as the reference does (4 bytes per scale)."""

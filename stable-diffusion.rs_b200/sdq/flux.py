@@ -92,6 +92,17 @@ def flops(cfg: FluxShape) -> float:
     return float(sum(2 * m * n * k for _, n, k, m in linear_table(cfg)))
 
 
+def output_stage(name: str) -> Tuple[Optional[str], bool]:
+    """(activation, gated residual update) fused into the linear's output stage in forward():
+    the MLP's first layer and the conditioning MLPs' inner layer apply an activation, and the
+    projections that feed the residual stream multiply by a modulation gate and add into it."""
+    if name.endswith("_mlp.0.weight"):
+        return "gelu_approx", False
+    if name.endswith(".in_layer.weight"):
+        return "silu", False
+    return None, bits_for(name) == 8
+
+
 def bits_for(name: str) -> int:
     """The whole-model configuration's policy: residual-multiplying projections 8 bits, the rest 4."""
     if name.endswith("_attn.proj.weight") or name.endswith("_mlp.2.weight") or name.endswith(".linear2.weight"):
@@ -206,7 +217,7 @@ def timestep_embedding(t, dim, theta):
 
 
 def mlp_embedder(w, x, prefix):
-    h = F.silu(w.linear(x, f"{prefix}.in_layer.weight", w.optional(f"{prefix}.in_layer.bias")))
+    h = w.linear_fused(x, f"{prefix}.in_layer.weight", w.optional(f"{prefix}.in_layer.bias"), act="silu")
     return w.linear(h, f"{prefix}.out_layer.weight", w.optional(f"{prefix}.out_layer.bias"))
 
 
@@ -235,13 +246,14 @@ def double_block(w, img, txt, vec, cos, sin, i, cfg: FluxShape):
     a = attention(q, k, v)
     nt = txt.shape[1]
 
+    # x + gate * linear(..) and gelu(linear(..)) run inside the linear's output stage.
     def finish(x, att, m, tag):
-        x = x + w.linear(att.contiguous(), f"{p}.{tag}_attn.proj.weight",
-                         w.optional(f"{p}.{tag}_attn.proj.bias")) * m[2]
-        ff = F.gelu(w.linear(norm_modulate(x, m[3], m[4]), f"{p}.{tag}_mlp.0.weight",
-                             w.optional(f"{p}.{tag}_mlp.0.bias")), approximate="tanh")
-        ff = w.linear(ff, f"{p}.{tag}_mlp.2.weight", w.optional(f"{p}.{tag}_mlp.2.bias"))
-        return x + ff * m[5]
+        x = w.linear_fused(att.contiguous(), f"{p}.{tag}_attn.proj.weight",
+                           w.optional(f"{p}.{tag}_attn.proj.bias"), gate=m[2], residual=x)
+        ff = w.linear_fused(norm_modulate(x, m[3], m[4]), f"{p}.{tag}_mlp.0.weight",
+                            w.optional(f"{p}.{tag}_mlp.0.bias"), act="gelu_approx")
+        return w.linear_fused(ff, f"{p}.{tag}_mlp.2.weight", w.optional(f"{p}.{tag}_mlp.2.bias"),
+                              gate=m[5], residual=x)
 
     return finish(img, a[:, nt:], im, "img"), finish(txt, a[:, :nt], tm, "txt")
 
@@ -255,8 +267,8 @@ def single_block(w, x, vec, cos, sin, i, cfg: FluxShape):
     q = rotate(qk_norm(q, w.dense_tensor(f"{p}.norm.query_norm.scale")), cos, sin)
     k = rotate(qk_norm(k, w.dense_tensor(f"{p}.norm.key_norm.scale")), cos, sin)
     joined = torch.cat((attention(q, k, v), F.gelu(proj[..., 3 * h:], approximate="tanh")), dim=2)
-    out = w.linear(joined, f"{p}.linear2.weight", w.optional(f"{p}.linear2.bias"))
-    return x + out * m[2]
+    return w.linear_fused(joined, f"{p}.linear2.weight", w.optional(f"{p}.linear2.bias"),
+                          gate=m[2], residual=x)
 
 
 def forward(w, img, txt, timestep, pooled, cfg: FluxShape, rope) -> torch.Tensor:
@@ -302,11 +314,20 @@ class LinearsOnly:
             if (m, k) not in xs:
                 xs[(m, k)] = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
             y = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-            self.calls.append((w.quantized[name], xs[(m, k)], w.optional(name[: -len("weight")] + "bias"), y))
+            act, gated = output_stage(name)
+            gate = resid = None
+            if gated:      # the forward's gate [n] and residual stream [m, n]
+                gate = torch.randn(n, device=device, generator=g).to(torch.bfloat16)
+                resid = torch.randn(m, n, device=device, generator=g).to(torch.bfloat16)
+            self.calls.append((w.quantized[name], xs[(m, k)], w.optional(name[: -len("weight")] + "bias"), y,
+                               act, gate, resid))
 
     def __call__(self) -> None:
-        for q, x, b, y in self.calls:
-            q.matmul(x, bias=b, out=y)
+        for q, x, b, y, act, gate, resid in self.calls:
+            if act is None and gate is None:
+                q.matmul(x, bias=b, out=y)
+            else:
+                q.matmul_fused(x, bias=b, act=act, gate=gate, residual=resid, out=y)
 
     def __iter__(self) -> Iterator:
         return iter(self.calls)

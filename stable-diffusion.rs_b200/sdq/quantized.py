@@ -11,8 +11,9 @@ from __future__ import annotations
 from typing import Callable, Dict, Mapping, Optional, Protocol
 
 import torch
+import torch.nn.functional as F
 
-from . import QuantizedArray, SdqError
+from . import ACT_GELU_TANH, ACT_NONE, ACT_SILU, QuantizedArray, SdqError
 from ._abi import SDQ_ERR_INVALID
 
 #: MLX's default group size; must divide the weight's input width (quantized.rs:45-46).
@@ -49,6 +50,11 @@ class QuantizedWeights:
     # WeightSource (quantized.rs:359-380)
     def linear(self, x: torch.Tensor, name: str, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
         return linear(x, name, bias, self)
+
+    def linear_fused(self, x: torch.Tensor, name: str, bias: Optional[torch.Tensor] = None, act=None,
+                     gate: Optional[torch.Tensor] = None,
+                     residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return linear_fused(x, name, bias, self, act, gate, residual)
 
     def dense_tensor(self, name: str) -> torch.Tensor:
         if name in self.dense:
@@ -132,10 +138,42 @@ def linear(x: torch.Tensor, name: str, bias: Optional[torch.Tensor], w: Quantize
     return dense_linear(x, d, bias)
 
 
+def apply_epilogue(y: torch.Tensor, act=None, gate: Optional[torch.Tensor] = None,
+                   residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The elementwise chain after a linear, one op at a time as the reference runs it:
+    ``gelu_approx`` / ``silu`` (flux.rs:400-407, 491-495), then ``.mul(gate)`` and
+    ``x.add(..)`` (flux.rs:389-398, 408-414, 470)."""
+    if act in ("gelu_approx", "gelu_tanh", ACT_GELU_TANH):
+        y = F.gelu(y, approximate="tanh")
+    elif act in ("silu", ACT_SILU):
+        y = F.silu(y)
+    elif act not in (None, "none", ACT_NONE):
+        raise SdqError(SDQ_ERR_INVALID, f"unknown activation {act!r}")
+    if gate is not None:
+        y = y * gate
+    if residual is not None:
+        y = residual + y
+    return y
+
+
+def linear_fused(x: torch.Tensor, name: str, bias: Optional[torch.Tensor], w: QuantizedWeights, act=None,
+                 gate: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``residual + gate * act(linear(x))``: one libsdq kernel when ``name`` is quantised, the
+    op-by-op chain otherwise."""
+    q = w.quantized.get(name)
+    if q is not None:
+        return q.matmul_fused(x, bias=bias, act=act, gate=gate, residual=residual)
+    return apply_epilogue(linear(x, name, bias, w), act, gate, residual)
+
+
 class WeightSource(Protocol):
     """Where a model's weights come from (quantized.rs:325-339)."""
 
     def linear(self, x: torch.Tensor, name: str, bias: Optional[torch.Tensor] = None) -> torch.Tensor: ...
+
+    def linear_fused(self, x: torch.Tensor, name: str, bias: Optional[torch.Tensor] = None, act=None,
+                     gate: Optional[torch.Tensor] = None,
+                     residual: Optional[torch.Tensor] = None) -> torch.Tensor: ...
 
     def dense_tensor(self, name: str) -> torch.Tensor: ...
 
@@ -149,6 +187,9 @@ class DenseWeights(dict):
         if name not in self:
             raise SdqError(SDQ_ERR_INVALID, f"mlx: missing tensor {name}")
         return dense_linear(x, self[name], bias)
+
+    def linear_fused(self, x, name, bias=None, act=None, gate=None, residual=None):
+        return apply_epilogue(self.linear(x, name, bias), act, gate, residual)
 
     def dense_tensor(self, name):
         if name not in self:

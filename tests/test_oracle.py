@@ -140,3 +140,29 @@ def test_oracle_rejects_what_the_reference_cannot_quantise():
         O.quantize(np.zeros((4, 100), np.float32), 4)   # K % 64 != 0 stays dense
     with pytest.raises(ValueError):
         O.quantize(np.zeros((4, 64), np.float32), 3)
+
+
+# ---------------------------------------------------------------- fused output stage
+
+def test_epilogue_activations_match_torch_independent_implementations():
+    """The oracle's gelu_approx / silu (restated from the reference's formulas) against torch's
+    own CPU implementations in f64."""
+    import torch
+    a = np.linspace(-12.0, 12.0, 4001).reshape(1, -1)
+    ta = torch.from_numpy(a)
+    g = O.epilogue(a, act=O.ACT_GELU_TANH)
+    s = O.epilogue(a, act=O.ACT_SILU)
+    assert np.max(np.abs(g - torch.nn.functional.gelu(ta, approximate="tanh").numpy())) < 1e-12
+    assert np.max(np.abs(s - torch.nn.functional.silu(ta).numpy())) < 1e-12
+    assert np.array_equal(O.epilogue(a), a)
+
+
+def test_epilogue_order_is_residual_plus_gate_times_activation_of_biased_product():
+    acc = np.array([[1.0, -2.0], [0.5, 3.0]], np.float32)
+    bias = O.f32_to_bf16_bits(np.array([0.5, 1.0], np.float32))
+    gate = O.f32_to_bf16_bits(np.array([2.0, -1.0], np.float32))
+    resid = O.f32_to_bf16_bits(np.array([[10.0, 20.0], [30.0, 40.0]], np.float32))
+    y = O.epilogue(acc, bias, O.ACT_SILU, gate, resid)
+    silu = lambda v: v / (1.0 + np.exp(-v))
+    want = np.array([[10 + 2 * silu(1.5), 20 - silu(-1.0)], [30 + 2 * silu(1.0), 40 - silu(4.0)]])
+    assert np.allclose(y, want, rtol=0, atol=1e-12)
