@@ -137,6 +137,11 @@ def cpu_reference(args, wl):
 
     if wl == "cfg4":
         return cpu_reference_flux(args, O)
+    if wl == "encoders":
+        sys.path.insert(0, os.path.join(ROOT, "stable-diffusion.rs_b200"))
+        from sdq import encoders as E
+        shapes = sorted({(n, k, 4) for e in E.ENCODERS for _, n, k, _ in E.layer_linears(e, 512)})
+        return cpu_reference_shapes(args, O, shapes, "text-encoder linear shapes (W4)")
     m, k, n, bits, sig, kind = WORKLOADS[wl]
     threads = O.max_threads()
     ms = min(m, 8 if kind == "gbs" else 48)     # sample rows of X per step
@@ -160,9 +165,14 @@ def cpu_reference(args, wl):
 def cpu_reference_flux(args, O):
     """The oracle over a sample of the Flux stack's linears: 16 rows of X through each distinct
     linear shape of a double block, a single block and a modulation, in TFLOP/s."""
-    threads = O.max_threads()
     shapes = [(9216, 3072, 4), (3072, 3072, 8), (12288, 3072, 4), (3072, 12288, 8),
               (21504, 3072, 4), (3072, 15360, 8), (18432, 3072, 4)]
+    return cpu_reference_shapes(args, O, shapes, "Flux linear shapes (W4/W8)")
+
+
+def cpu_reference_shapes(args, O, shapes, label):
+    """16 rows of X through each (N, K, bits) of ``shapes`` on all host threads, in TFLOP/s."""
+    threads = O.max_threads()
     ms = 16
     cases = []
     for i, (n, k, bits) in enumerate(shapes):
@@ -177,7 +187,7 @@ def cpu_reference_flux(args, O):
             times.append(time.perf_counter() - t0)
     flops = sum(c[4] for c in cases)
     t = statistics.median(times)
-    sample = f"16 rows of X through each of {len(shapes)} Flux linear shapes (W4/W8); median of {len(times)}"
+    sample = f"16 rows of X through each of {len(shapes)} {label}; median of {len(times)}"
     return flops / t / 1e12, threads, sample
 
 
@@ -216,14 +226,22 @@ def run_flux(args, rank, world, local):
         lin()
         flux.forward(qw, *ins, cfg, rope)
     sdq.device_status()
-    g_lin, g_fwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    # The same forward with each linear's elementwise consumers run op by op (the reference's
+    # way), to show what the fused output stage saves.
+    from sdq.quantized import OpByOp
+    opw = OpByOp(qw)
+    flux.forward(opw, *ins, cfg, rope)
+    g_lin, g_fwd, g_op = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_lin):
         lin()
     with torch.cuda.graph(g_fwd):
         out = flux.forward(qw, *ins, cfg, rope)
+    with torch.cuda.graph(g_op):
+        flux.forward(opw, *ins, cfg, rope)
     for _ in range(2):
         g_lin.replay()
         g_fwd.replay()
+        g_op.replay()
     barrier()
     sdq.device_status()
 
@@ -245,7 +263,9 @@ def run_flux(args, rank, world, local):
     with ClockSampler(local) as clk:
         lin_ms = timed(g_lin.replay, args.steps)
     fwd_ms = timed(g_fwd.replay, args.steps)
+    op_ms = timed(g_op.replay, args.steps)
     sdq.device_status()
+    del g_op
 
     # end to end: the eager forward through the public API with host inputs and output
     hosts = [t.cpu().pin_memory() for t in ins]
@@ -280,10 +300,12 @@ def run_flux(args, rank, world, local):
             "data": "synthetic (seeded random-init Flux-shaped weights, quantised by libsdq)",
             "config": {"workload": "cfg4",
                        "descr": "config 4: Flux-schnell-shaped stack, 19 double + 38 single blocks, "
-                                "512 txt + 4096 img tokens, hidden 3072, out-proj/MLP-down W8, rest W4",
+                                "512 txt + 4096 img tokens, hidden 3072, out-proj/MLP-down W8, rest W4; "
+                                "gate/residual and GELU/SiLU fused into the linears' output stage",
                        "linears": len(flux.linear_table(cfg)), "qmm_tflop_per_forward": total_flops / 1e12,
                        "packed_weight_bytes": qw.resident_bytes(),
                        "forward_ms": fwd_ms, "qmm_share_of_forward": lin_ms / fwd_ms,
+                       "forward_op_by_op_ms": op_ms,
                        "parallelism": "single GPU" if world == 1 else f"{world} replicas",
                        "l2": "weights (8.5 GB) exceed L2; 256 MiB write before every step anyway"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc, "unit": "TFLOP/s",
@@ -300,12 +322,138 @@ def run_flux(args, rank, world, local):
         }))
 
 
+def run_encoders(args, rank, world, local):
+    """The text encoders' layers (T5-XXL, Qwen3-4B, Qwen2.5-VL-7B, Mistral Small 3.2; W4) at 512
+    prompt tokens: one layer's linears per encoder, each encoder's set captured in a CUDA graph.
+    N > 1 runs independent replicas; the time is the max over ranks."""
+    import torch
+    import sdq
+    from sdq import encoders as E
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    tokens, bits = 512, 4
+    g = torch.Generator(device=dev).manual_seed(21)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    sets = []
+    for e in E.ENCODERS:
+        calls = []
+        for name, n, k, m in E.layer_linears(e, tokens):
+            wq, s, b = sdq.quantize(torch.randn(n, k, device=dev, generator=g) * 0.02, 64, bits)
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            calls.append((x, wq, s, b, torch.empty(m, n, device=dev, dtype=torch.bfloat16)))
+        sets.append((e, calls, E.flops(E.layer_linears(e, tokens))))
+
+    def run(calls):
+        for x, wq, s, b, y in calls:
+            sdq.quantized_matmul(x, wq, s, b, 64, bits, out=y)
+
+    graphs = []
+    for e, calls, fl in sets:
+        for _ in range(args.warmup):
+            run(calls)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            run(calls)
+        graphs.append(gr)
+    sdq.device_status()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(fn, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        barrier()
+        t = sum(a.elapsed_time(b) for a, b in ev)
+        if dist is not None:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t / steps
+
+    def all_layers():
+        for gr in graphs:
+            gr.replay()
+
+    barrier()
+    with ClockSampler(local) as clk:
+        step_ms = timed(all_layers, args.steps)
+    per = {e.name: {"ms": timed(gr.replay, args.steps), "gflop": fl / 1e9}
+           for (e, _, fl), gr in zip(sets, graphs)}
+    for v in per.values():
+        v["tflops"] = v["gflop"] / v["ms"]
+    sdq.device_status()
+    total = sum(fl for _, _, fl in sets)
+
+    # end to end: each layer's input from pinned host memory, its last output back, eager calls
+    hosts = [[c[0].cpu().pin_memory() for c in calls] for _, calls, _ in sets]
+    outs = [torch.empty(tuple(calls[-1][4].shape), dtype=torch.bfloat16, pin_memory=True) for _, calls, _ in sets]
+
+    def e2e_step():
+        for (_, calls, _), hs, oh in zip(sets, hosts, outs):
+            for c, h in zip(calls, hs):
+                c[0].copy_(h, non_blocking=True)
+            run(calls)
+            oh.copy_(calls[-1][4], non_blocking=True)
+
+    e2e_step()
+    e2e_ms = timed(e2e_step, args.steps)
+    hbm, tc, src = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cv, threads, sample = cpu_reference(argparse.Namespace(steps=3, warmup=3), "encoders")
+        cpu = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
+    del graphs
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        achieved = total / (step_ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "qmatmul_tflops", "value": total * world / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights of each encoder's shapes, quantised by libsdq)",
+            "config": {"workload": "encoders",
+                       "descr": "one layer's linears of T5-XXL, Qwen3-4B, Qwen2.5-VL-7B and Mistral Small 3.2 "
+                                "at 512 prompt tokens, W4 g64",
+                       "per_encoder": per, "tokens": tokens,
+                       "parallelism": "single GPU" if world == 1 else f"{world} replicas",
+                       "l2": "256 MiB write before every step"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc, "unit": "TFLOP/s",
+                         "frac": achieved / tc, "peak_source": f"{src} burst bf16 (MEASURED_PEAKS.json)",
+                         "traffic": None, "kernel_ms": step_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": sum(h.numel() * 2 for hs in hosts for h in hs),
+                    "d2h_bytes_per_step": sum(o.numel() * 2 for o in outs),
+                    "path": "sdq.quantized_matmul per linear, inputs from and last output to pinned host"},
+            "gpu_launches": args.steps * sum(len(c) for _, c, _ in sets),
+            "clocks": clk.summary(),
+        }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="cfg2", choices=sorted(list(WORKLOADS) + ["cfg4"]))
+    ap.add_argument("--workload", default="cfg2", choices=sorted(list(WORKLOADS) + ["cfg4", "encoders"]))
     ap.add_argument("--impl", default="sdq", choices=["sdq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -315,7 +463,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     wl = args.workload
-    kind = "tflops" if wl == "cfg4" else WORKLOADS[wl][5]
+    kind = "tflops" if wl in ("cfg4", "encoders") else WORKLOADS[wl][5]
     metric = "qmatmul_tflops" if kind == "tflops" else "qmatmul_hbm_gbs"
     unit = "TFLOP/s" if kind == "tflops" else "GB/s"
 
@@ -327,7 +475,8 @@ def main():
             "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (SeededRng)",
-            "config": {"workload": wl, "descr": DESCR.get(wl, "config 4: Flux-shaped stack"),
+            "config": {"workload": wl, "descr": DESCR.get(wl, "config 4: Flux-shaped stack" if wl == "cfg4"
+                                                          else "text-encoder layers at 512 tokens"),
                        "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                              "sample": sample},
@@ -336,6 +485,8 @@ def main():
         return
     if wl == "cfg4":
         return run_flux(args, rank, world, local)
+    if wl == "encoders":
+        return run_encoders(args, rank, world, local)
     m, k, n, bits, sig, kind = WORKLOADS[wl]
 
     import torch

@@ -166,6 +166,26 @@ def linear_fused(x: torch.Tensor, name: str, bias: Optional[torch.Tensor], w: Qu
     return apply_epilogue(linear(x, name, bias, w), act, gate, residual)
 
 
+class OpByOp:
+    """A weight source whose ``linear_fused`` runs the linear and then the elementwise chain
+    op by op, as the reference does -- for measuring what the fused output stage saves."""
+
+    def __init__(self, inner):
+        self.inner = inner
+
+    def linear(self, x, name, bias=None):
+        return self.inner.linear(x, name, bias)
+
+    def linear_fused(self, x, name, bias=None, act=None, gate=None, residual=None):
+        return apply_epilogue(self.inner.linear(x, name, bias), act, gate, residual)
+
+    def dense_tensor(self, name):
+        return self.inner.dense_tensor(name)
+
+    def optional(self, name):
+        return self.inner.optional(name)
+
+
 class WeightSource(Protocol):
     """Where a model's weights come from (quantized.rs:325-339)."""
 

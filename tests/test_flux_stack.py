@@ -41,3 +41,23 @@ def test_small_stack_quantised_forward_matches_the_dense_forward():
     cos = float(g @ w / (g.norm() * w.norm()))
     rel = float((g - w).abs().max() / w.abs().max())
     assert cos >= 0.999 and rel <= 5e-2, (cos, rel)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not gpu_available(), reason="needs an sm_100 device")
+def test_fused_output_stages_match_the_op_by_op_forward():
+    """The forward with gate / residual / activation fused into the linears against the same
+    quantised weights with those ops run one by one after each linear."""
+    from sdq.quantized import OpByOp
+    cfg = flux.FluxShape(hidden=256, heads=2, depth=2, depth_single=2, txt_tokens=32, img_tokens=64,
+                         context_dim=128, vec_dim=64)
+    qw = flux.random_weights(cfg, seed=5)
+    rope = flux.rope_tables(cfg)
+    args = flux.inputs(cfg, seed=6)
+    got = flux.forward(qw, *args, cfg, rope)
+    want = flux.forward(OpByOp(qw), *args, cfg, rope)
+    torch.cuda.synchronize()
+    g, w = got.double().flatten(), want.double().flatten()
+    cos = float(g @ w / (g.norm() * w.norm()))
+    rel = float((g - w).abs().max() / w.abs().max())
+    assert cos >= 0.999 and rel <= 5e-2, (cos, rel)
