@@ -51,7 +51,11 @@ struct Comm {
     int device = 0;
     // Overlapped exchange (set up when world > 1; the plain path runs without it).
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_bar = nullptr;
+    // One push stream per peer, so that the pushes to different peers run concurrently
+    // on different copy engines (one stream runs its copies one after another).
+    cudaStream_t push[kMaxWorld] = {};
+    cudaEvent_t push_done[kMaxWorld] = {};
     uint32_t* counters = nullptr;          // kMaxChunks completion counts + 1 barrier word
     // This rank's exchange buffer ([world, m, n_local] bf16; peers push into it) and the
     // peers' buffers as mapped here.
@@ -60,6 +64,18 @@ struct Comm {
     void* peer_xbuf[kMaxWorld] = {};
     cudaIpcMemHandle_t* handles_dev = nullptr;   // world handles, for the one-off exchange
 };
+
+void destroy_push_streams(Comm* c) {
+    for (int p = 0; p < kMaxWorld; ++p) {
+        if (c->push[p]) {
+            cudaStreamSynchronize(c->push[p]);
+            cudaStreamDestroy(c->push[p]);
+        }
+        if (c->push_done[p]) cudaEventDestroy(c->push_done[p]);
+        c->push[p] = nullptr;
+        c->push_done[p] = nullptr;
+    }
+}
 
 using ValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 
@@ -230,7 +246,10 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     const int64_t bt = sdq::qmm_tc_tile_tokens(m, k, n_local, bits, 0);
     const int64_t ntt = (m + bt - 1) / bt;
     if (ntt < 2) return kNotOverlapped;
-    int64_t nch = ntt < kChunks ? ntt : kChunks;
+    // Fewer, larger chunks when there are many peers: every chunk costs a wait and a copy
+    // per peer to enqueue.
+    const int64_t want_chunks = c->world <= 2 ? kChunks : kChunks / 2;
+    int64_t nch = ntt < want_chunks ? ntt : want_chunks;
     const int64_t tpc = (ntt + nch - 1) / nch;           // token tiles per chunk
     nch = (ntt + tpc - 1) / tpc;
     const int64_t nft = (n_local + 127) / 128;
@@ -247,9 +266,15 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     // anyone pushes into it again.
     ncclResult_t r = side_barrier(c, c->side);
     if (r != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
-    cudaError_t e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
+    cudaError_t e = cudaEventRecord(c->ev_bar, c->side);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = cudaEventRecord(c->ev_start, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->ev_start, 0);
+    // The pushes follow the barrier (side) and the counters' reset (st).
+    for (int p = 0; e == cudaSuccess && p < c->world; ++p) {
+        if (p == c->rank) continue;
+        e = cudaStreamWaitEvent(c->push[p], c->ev_bar, 0);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0);
+    }
     if (e != cudaSuccess) return cuda_err("stream set-up", e);
     const char* msg = nullptr;
     e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits,
@@ -262,30 +287,36 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         }
         return cuda_err("tensor-core kernel", e);
     }
-    bool waited_all = false;
+    // Without stream memory operations every push waits for the whole kernel instead.
+    if (wait == nullptr) {
+        if ((e = cudaEventRecord(c->ev_start, st)) != cudaSuccess) return cuda_err("stream wait", e);
+        for (int p = 0; p < c->world; ++p)
+            if (p != c->rank && (e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0)) != cudaSuccess)
+                return cuda_err("stream wait", e);
+    }
     for (int64_t i = 0; i < nch; ++i) {
         const int64_t t0 = i * tpc, t1 = (i + 1) * tpc < ntt ? (i + 1) * tpc : ntt;
         const int64_t m0 = t0 * bt, m1 = t1 * bt < m ? t1 * bt : m;
         const cuuint32_t target = static_cast<cuuint32_t>((t1 - t0) * nft);
-        if (!waited_all &&
-            (wait == nullptr ||
-             wait(reinterpret_cast<CUstream>(c->side), reinterpret_cast<CUdeviceptr>(c->counters + i),
-                  target, 0 /* GEQ */) != CUDA_SUCCESS)) {
-            // No stream memory operations: wait for the whole kernel instead.
-            if ((e = cudaEventRecord(c->ev_start, st)) != cudaSuccess ||
-                (e = cudaStreamWaitEvent(c->side, c->ev_start, 0)) != cudaSuccess)
-                return cuda_err("stream wait", e);
-            waited_all = true;
-        }
         const size_t off = static_cast<size_t>(m0) * n_local;
         const size_t bytes = static_cast<size_t>(m1 - m0) * n_local * sizeof(uint16_t);
         for (int p = 0; p < c->world; ++p) {
             if (p == c->rank) continue;
+            if (wait != nullptr &&
+                wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->counters + i),
+                     target, 0 /* GEQ */) != CUDA_SUCCESS)
+                return cuda_err("stream wait on a chunk count", cudaErrorUnknown);
             uint16_t* dst = static_cast<uint16_t*>(c->peer_xbuf[p]) + c->rank * block + off;
-            if ((e = cudaMemcpyAsync(dst, mine + off, bytes, cudaMemcpyDeviceToDevice, c->side)) !=
+            if ((e = cudaMemcpyAsync(dst, mine + off, bytes, cudaMemcpyDeviceToDevice, c->push[p])) !=
                 cudaSuccess)
                 return cuda_err("push to a peer", e);
         }
+    }
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        if ((e = cudaEventRecord(c->push_done[p], c->push[p])) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(c->side, c->push_done[p], 0)) != cudaSuccess)
+            return cuda_err("push join", e);
     }
     // All pushes into this rank's buffer have landed once every rank has passed here.
     if ((r = side_barrier(c, c->side)) != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
@@ -340,16 +371,25 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
     }
     if (world > 1) {
         // Resources of the overlapped exchange; if any is missing the plain path runs.
-        bool okr = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
+        bool okr = world <= kMaxWorld &&
+                   cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&c->ev_bar, cudaEventDisableTiming) == cudaSuccess &&
                    cudaMalloc(reinterpret_cast<void**>(&c->counters), (kMaxChunks + 1) * sizeof(uint32_t)) ==
                        cudaSuccess &&
                    world <= kMaxWorld &&
                    cudaMalloc(reinterpret_cast<void**>(&c->handles_dev), world * sizeof(cudaIpcMemHandle_t)) ==
                        cudaSuccess;
+        for (int p = 0; okr && p < world; ++p)
+            okr = p == rank ||
+                  (cudaStreamCreateWithFlags(&c->push[p], cudaStreamNonBlocking) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&c->push_done[p], cudaEventDisableTiming) == cudaSuccess);
         if (!okr) {
             cudaGetLastError();
+            destroy_push_streams(c);
+            if (c->ev_bar) cudaEventDestroy(c->ev_bar);
+            c->ev_bar = nullptr;
             if (c->handles_dev) cudaFree(c->handles_dev);
             if (c->counters) cudaFree(c->counters);
             if (c->ev_end) cudaEventDestroy(c->ev_end);
@@ -375,6 +415,8 @@ int sdq_comm_destroy(void* comm) {
         if (c->xbuf) cudaFree(c->xbuf);
         cudaFree(c->handles_dev);
         cudaFree(c->counters);
+        destroy_push_streams(c);
+        cudaEventDestroy(c->ev_bar);
         cudaEventDestroy(c->ev_end);
         cudaEventDestroy(c->ev_start);
         cudaStreamDestroy(c->side);
