@@ -516,7 +516,8 @@ def main():
         dist.broadcast_object_list(uid, src=0)
         comm = sdq.Comm(uid[0], world, rank)
         y_shards = torch.empty((world, m, n), device=dev, dtype=torch.bfloat16)
-        y_full = torch.empty((m, world * n), device=dev, dtype=torch.bfloat16)
+        # The communicator's symmetric output: the peers' blocks land in place (no final copy).
+        y_full = comm.output(m, world * n)
     y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
 
     def step():
@@ -638,7 +639,8 @@ def main():
             "data": "synthetic (seeded torch normal; weights quantised by libsdq)",
             "config": {"workload": wl, "descr": DESCR[wl], "M": m, "K": k, "N_per_rank": n, "bits": bits,
                        "group_size": 64, "global_N": n * world,
-                       "parallelism": "single GPU" if world == 1 else f"N-sharded x{world} + NCCL all-gather",
+                       "parallelism": "single GPU" if world == 1 else
+                           f"N-sharded x{world}; output blocks pushed by copy engines over NVLink during the compute",
                        "l2": "flushed before every step (256 MiB write, outside the timed events)"},
             "roofline": roof,
             "cpu_baseline": cpu,
@@ -646,7 +648,9 @@ def main():
                     "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * world * 2,
                     "path": "sdq.quantized_matmul%s (C ABI) with pinned host X in, Y out" %
                             ("" if world == 1 else "_sharded")},
-            "gpu_launches": args.steps * (1 if world == 1 else 2),
+            # N > 1: the overlapped path (M > 8) runs only the tensor-core kernel (the peers'
+            # blocks arrive by copy engine into the communicator's output); M <= 8 adds the permute.
+            "gpu_launches": args.steps * (1 if world == 1 or m > 8 else 2),
             "clocks": clk.summary(),
         }
         print(json.dumps(line))

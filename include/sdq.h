@@ -180,17 +180,32 @@ int sdq_comm_destroy(void* comm);
  * permutes that into y[m, world*n_local].  y_shards is caller-provided
  * (world*m*n_local elements, 16-byte aligned).  The compute step is
  * sdq_quantized_matmul; the exchange is one ncclAllGather on `stream`.
- * When y is non-NULL, world > 1 and M spans several token tiles, the exchange
- * instead overlaps the compute: finished row chunks are pushed by the copy
- * engines into the peers' library-owned exchange buffers (allocated on the
- * first such call, grown when a call needs more) and y_shards then holds only
- * this rank's block on return.  Every rank must make the same calls.
+ * When y is non-NULL, world > 1, n_local % 8 == 0 and M spans several token
+ * tiles, the exchange instead overlaps the compute: the kernel writes this
+ * rank's column block of the communicator's output buffer (see
+ * sdq_comm_output) and the copy engines push finished row chunks of it into
+ * the same place of every peer's buffer; the assembled [m, world*n_local] is
+ * then copied to y, unless y is that buffer.  y_shards is not written on this
+ * path.  Every rank must make the same calls, in the same order.
  */
 int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                                  const uint32_t* wq, const void* scales, const void* biases,
                                  sdq_dtype sb_dtype, int64_t n_local, int group_size, int bits,
                                  const void* bias_local, void* y_shards, void* y,
                                  sdq_dtype y_dtype, void* comm, void* stream);
+
+/*
+ * The communicator's output buffer: device memory of at least m*n bf16 values
+ * on this rank, mapped into every peer (IPC), which the overlapped sharded call
+ * assembles its [m, n] result in.  Passing it as that call's y leaves the
+ * result there with no final copy.  Collective: every rank calls it with the
+ * same m, n.  The pointer stays valid until a later call needs a larger buffer
+ * (sdq_comm_output or a sharded call with a larger output, which reallocates)
+ * or the communicator is destroyed; each sharded call overwrites its contents.
+ * A sharded call whose y lies in the buffer but does not fit in it fails with
+ * SDQ_ERR_INVALID.  No counterpart in the reference (single-device).
+ */
+int sdq_comm_output(void* comm, int64_t m, int64_t n, void** out);
 
 /*
  * sdq_quantized_matmul_sharded without the caller's y_shards buffer, for callers

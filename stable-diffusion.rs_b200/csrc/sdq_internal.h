@@ -56,14 +56,15 @@ int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const u
                  const void* y, sdq_dtype y_dtype, const char* fn);
 
 // The tensor-core matmul for the overlapped sharded linear: the same kernel, on at most
-// grid_cap CTAs (0: every SM), adding 1 to done[tt / chunk_tts] once token tile tt's output
-// tile is in global memory (nchunks counters).  qmm_tc_tile_tokens is the token-tile height
-// the dispatcher picks for the shape.
+// grid_cap CTAs (0: every SM), writing rows ldy elements apart and adding 1 to
+// done[tt / chunk_tts] once token tile tt's output tile is in global memory (nchunks
+// counters).  qmm_tc_tile_tokens is the token-tile height the dispatcher picks for the shape.
 int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap);
 cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                                  const void* scales, const void* biases, int64_t n, int bits,
-                                 const EpiArgs& epi, void* y, cudaStream_t st, const char** msg,
-                                 uint32_t* done, int chunk_tts, int nchunks, int grid_cap);
+                                 const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
+                                 const char** msg, uint32_t* done, int chunk_tts, int nchunks,
+                                 int grid_cap);
 
 // Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs).
 // Sets *taken = false, launching nothing, for shapes it does not serve (M > 8, or X too

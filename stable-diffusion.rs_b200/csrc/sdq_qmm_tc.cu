@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
                   const uint16_t* __restrict__ biases, const EpiArgs epi,
-                  uint16_t* y, int M, int N, int K, int y_tma, int r_tma,
+                  uint16_t* y, int M, int N, int K, int64_t ldy, int y_tma, int r_tma,
                   const TcSignal sig) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                         reinterpret_cast<const uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
                     const int t0 = tt * BT + c * CW;
                     const int nr = M - t0 < CW ? M - t0 : CW;
-                    for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * N + f] = yrow[r * C::BF];
+                    for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * ldy + f] = yrow[r * C::BF];
                 }
             }
             if (sig.done != nullptr) {
@@ -503,8 +503,8 @@ constexpr size_t kMaxSmem = kQmvMaxSmem;
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                        const void* biases, int64_t n, const EpiArgs& epi, void* y, cudaStream_t st,
-                        const char** msg, const TcSignal& sig, int grid_cap) {
+                        const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
+                        cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     auto enc = tensor_map_encoder();
     if (!enc) {
@@ -540,14 +540,14 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
             return cudaErrorInvalidValue;
         }
     }
-    // Y is written by TMA tensor stores when its row pitch and base are 16-byte
-    // aligned; otherwise the tensor map stays unused and the epilogue stores.
+    // Y (rows ldy elements apart) is written by TMA tensor stores when its row pitch and
+    // base are 16-byte aligned; otherwise the tensor map stays unused and the epilogue stores.
     CUtensorMap tmY;
     std::memset(&tmY, 0, sizeof(tmY));
-    const bool y_tma = (n % 8) == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+    const bool y_tma = (ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
     if (y_tma) {
         cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
-        cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+        cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
         cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)C::CW};
         cuuint32_t estr[2] = {1, 1};
         CUresult r = enc(&tmY, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, dims, strides, box, estr,
@@ -558,10 +558,11 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
             return cudaErrorInvalidValue;
         }
     }
-    // The residual, same geometry as Y, is copied in by TMA under the same conditions.
+    // The residual ([m, n], contiguous) is copied in by TMA under the same conditions.
     CUtensorMap tmR;
     std::memset(&tmR, 0, sizeof(tmR));
-    const bool r_tma = y_tma && epi.resid != nullptr && (reinterpret_cast<uintptr_t>(epi.resid) % 16) == 0;
+    const bool r_tma = y_tma && n % 8 == 0 && epi.resid != nullptr &&
+                       (reinterpret_cast<uintptr_t>(epi.resid) % 16) == 0;
     if (r_tma) {
         cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
         cuuint64_t strides[1] = {(cuuint64_t)n * 2};
@@ -593,7 +594,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
-        y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
+        ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
     return cudaGetLastError();
 }
 
@@ -630,19 +631,19 @@ int choose_tile(int64_t m, int64_t k, int64_t n, int grid_cap) {
 template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                            const void* scales, const void* biases, int64_t n, const EpiArgs& epi,
-                           void* y, cudaStream_t st, const char** msg, const TcSignal& sig,
+                           void* y, int64_t ldy, cudaStream_t st, const char** msg, const TcSignal& sig,
                            int grid_cap) {
     // Ring depths fill the shared memory budget; the packed-weight ring is the deep one.
     constexpr int SWs = BITS == 4 ? 16 : 12;
     constexpr int SWL = BITS == 4 ? 8 : 4;
     switch (choose_tile<BITS>(m, k, n, grid_cap)) {
-        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
-        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
     }
 }
 
@@ -665,8 +666,8 @@ cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* w
                           const void* scales, const void* biases, int64_t n, int bits,
                           const EpiArgs& epi, void* y, cudaStream_t st, const char** msg) {
     const TcSignal off{nullptr, 1, 0};
-    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, off, 0)
-                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, off, 0);
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, n, st, msg, off, 0)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, n, st, msg, off, 0);
 }
 
 int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) {
@@ -676,11 +677,12 @@ int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) 
 
 cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                                  const void* scales, const void* biases, int64_t n, int bits,
-                                 const EpiArgs& epi, void* y, cudaStream_t st, const char** msg,
-                                 uint32_t* done, int chunk_tts, int nchunks, int grid_cap) {
+                                 const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
+                                 const char** msg, uint32_t* done, int chunk_tts, int nchunks,
+                                 int grid_cap) {
     const TcSignal sig{done, chunk_tts, nchunks};
-    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap)
-                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, sig, grid_cap);
+    return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap)
+                     : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
 }
 
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st) {

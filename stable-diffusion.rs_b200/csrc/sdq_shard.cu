@@ -6,21 +6,22 @@
 // permute kernel turns that into [m, n].
 //
 // When the output is wanted as [m, n] on two or more ranks and M spans several
-// token tiles, the exchange overlaps the compute and uses no SMs: the tensor-core
-// kernel counts, per chunk of token tiles, the output tiles it has finished; a
-// library-owned side stream waits on each chunk's count (cuStreamWaitValue32) and
-// pushes that chunk's rows with the copy engines straight into every peer's
-// exchange buffer (IPC-mapped device memory, over NVLink) while the kernel computes
-// the next chunk -- without SMs.  A small NCCL all-reduce then tells each rank that
-// all pushes into its buffer have landed, and one permute kernel builds [m, n].
-// (NCCL's send / receive kernels did not start until the compute kernel had
-// finished, so they could not overlap it; per-chunk arrival flags with strided
-// copies into Y were slower than the single permute.)  A kernel that gives up
-// raises every count to its maximum, so the side stream never waits for ever.  The
-// exchange buffer is allocated on the first overlapped call and grows collectively
-// (every rank calls with the same shapes); a second small all-reduce at the start
-// of each call keeps a fast rank from pushing into a buffer that a slower one is
-// still permuting.
+// token tiles, the exchange overlaps the compute and uses no SMs.  Every rank owns a
+// symmetric output buffer ([m, n] bf16, IPC-mapped on every peer).  The tensor-core
+// kernel writes this rank's column block of it in place (rows world * n_local apart)
+// and counts, per chunk of token tiles, the output tiles it has finished; one push
+// stream per peer waits on each chunk's count (cuStreamWaitValue32) and copies that
+// chunk's rows of the column block, as one 2-D copy on the copy engines, into the
+// same place of the peer's buffer over NVLink while the kernel computes the next
+// chunk.  A small NCCL all-reduce then tells each rank that every push into its
+// buffer has landed: the buffer holds [m, n], and is copied to the caller's y unless y
+// is that buffer (sdq_comm_output).  (NCCL's send / receive kernels did not start
+// until the compute kernel had finished, so they could not overlap it.)  A kernel that
+// gives up raises every count to its maximum, so no push stream waits for ever.  The
+// buffer is allocated on first use and grows collectively (every rank calls with the
+// same shapes); a second all-reduce at the start of each call, entered once the
+// caller's stream has drained, keeps a fast rank from pushing into a buffer whose
+// previous contents a slower rank is still reading.
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -51,14 +52,15 @@ struct Comm {
     int device = 0;
     // Overlapped exchange (set up when world > 1; the plain path runs without it).
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_bar = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_bar = nullptr, ev_entry = nullptr,
+                ev_kernel = nullptr;
     // One push stream per peer, so that the pushes to different peers run concurrently
     // on different copy engines (one stream runs its copies one after another).
     cudaStream_t push[kMaxWorld] = {};
     cudaEvent_t push_done[kMaxWorld] = {};
     uint32_t* counters = nullptr;          // kMaxChunks completion counts + 1 barrier word
-    // This rank's exchange buffer ([world, m, n_local] bf16; peers push into it) and the
-    // peers' buffers as mapped here.
+    // The symmetric output: this rank's [m, n] bf16 buffer, into whose column blocks the
+    // kernel and the peers write, and the peers' buffers as mapped here.
     void* xbuf = nullptr;
     size_t xbuf_cap = 0;
     void* peer_xbuf[kMaxWorld] = {};
@@ -169,6 +171,16 @@ static int ensure_exchange_buffer(Comm* c, size_t bytes, const char* fn) {
         t_shard_msg = std::string(fn) + ": exchange buffer: " + what + ": " + cudaGetErrorString(e);
         return sdq::set_error_message(SDQ_ERR_CUDA, t_shard_msg.c_str());
     };
+    if (c->side == nullptr) {             // one rank, or no overlap resources: plain memory
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return fail_cuda("synchronise", e);
+        if (c->xbuf) cudaFree(c->xbuf);
+        c->xbuf = nullptr;
+        c->xbuf_cap = 0;
+        if ((e = cudaMalloc(&c->xbuf, bytes)) != cudaSuccess) return fail_cuda("cudaMalloc", e);
+        c->xbuf_cap = bytes;
+        return SDQ_OK;
+    }
     cudaError_t e = cudaStreamSynchronize(c->side);
     if (e != cudaSuccess) return fail_cuda("synchronise", e);
     for (int p = 0; p < c->world; ++p)
@@ -204,31 +216,16 @@ static int ensure_exchange_buffer(Comm* c, size_t bytes, const char* fn) {
     return SDQ_OK;
 }
 
-// y[t, p * nl + j] = (p == rank ? own : xbuf[p])[t, j]: the permute of the overlapped path,
-// which reads this rank's block from y_shards and the peers' blocks from the exchange buffer.
-__global__ void permute_exchange_v8(const uint4* __restrict__ xbuf, const uint4* __restrict__ own,
-                                    uint4* __restrict__ y, int64_t m, int64_t nl8, int world, int rank) {
-    const int64_t total = (int64_t)world * m * nl8;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i % nl8;
-        const int64_t t = (i / nl8) % m;
-        const int64_t r = i / (nl8 * m);
-        const uint4 v = r == rank ? own[t * nl8 + j] : xbuf[(r * m + t) * nl8 + j];
-        y[t * (world * nl8) + r * nl8 + j] = v;
-    }
+// Contiguous bf16 copy, 16 bytes per thread: the symmetric output -> the caller's y.
+__global__ void copy_v8(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n8) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
 }
-__global__ void permute_exchange_v1(const uint16_t* __restrict__ xbuf, const uint16_t* __restrict__ own,
-                                    uint16_t* __restrict__ y, int64_t m, int64_t nl, int world, int rank) {
-    const int64_t total = (int64_t)world * m * nl;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i % nl;
-        const int64_t t = (i / nl) % m;
-        const int64_t r = i / (nl * m);
-        const uint16_t v = r == rank ? own[t * nl + j] : xbuf[(r * m + t) * nl + j];
-        y[t * (world * nl) + r * nl + j] = v;
-    }
+__global__ void copy_v1(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
 }
 
 // The overlapped form of sdq_quantized_matmul_sharded (see the file comment).  Returns
@@ -236,14 +233,18 @@ __global__ void permute_exchange_v1(const uint16_t* __restrict__ xbuf, const uin
 static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                               const uint32_t* wq, const void* scales, const void* biases,
                               sdq_dtype sb_dtype, int64_t n_local, int group_size, int bits,
-                              const void* bias_local, void* y_shards, void* y, sdq_dtype y_dtype,
-                              void* stream) {
+                              const void* bias_local, void* y, sdq_dtype y_dtype, void* stream) {
     const char* fn = "sdq_quantized_matmul_sharded";
-    uint16_t* mine = static_cast<uint16_t*>(y_shards) + static_cast<size_t>(c->rank) * m * n_local;
+    const int64_t ldy = static_cast<int64_t>(c->world) * n_local;      // row pitch of [m, n]
     int rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n_local, 1, group_size,
-                               bits, "affine", bias_local, mine, y_dtype, fn);
+                               bits, "affine", bias_local, y, y_dtype, fn);
     if (rc != SDQ_OK) return rc;
-    const int64_t bt = sdq::qmm_tc_tile_tokens(m, k, n_local, bits, 0);
+    if ((n_local * 2) % 16 != 0) return kNotOverlapped;   // 2-D pushes want 16-byte rows
+    // The start barrier's NCCL kernel is enqueued as the compute kernel starts; the compute
+    // kernel keeps one SM free for it (a persistent kernel on every SM would hold the
+    // barrier, and every push behind it, until the compute had finished).
+    const int grid_cap = sdq::num_sms() - 1;
+    const int64_t bt = sdq::qmm_tc_tile_tokens(m, k, n_local, bits, grid_cap);
     const int64_t ntt = (m + bt - 1) / bt;
     if (ntt < 2) return kNotOverlapped;
     // Fewer, larger chunks when there are many peers: every chunk costs a wait and a copy
@@ -253,33 +254,39 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     const int64_t tpc = (ntt + nch - 1) / nch;           // token tiles per chunk
     nch = (ntt + tpc - 1) / tpc;
     const int64_t nft = (n_local + 127) / 128;
-    const size_t block = static_cast<size_t>(m) * n_local;   // elements of one rank's block
-    if ((rc = ensure_exchange_buffer(c, c->world * block * sizeof(uint16_t), fn)) != SDQ_OK) return rc;
-    uint16_t* xb = static_cast<uint16_t*>(c->xbuf);
+    const size_t total = static_cast<size_t>(m) * ldy;   // elements of [m, n]
+    if ((rc = ensure_exchange_buffer(c, total * sizeof(uint16_t), fn)) != SDQ_OK) return rc;
+    uint16_t* out = static_cast<uint16_t*>(c->xbuf);     // this rank's copy of [m, n]
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto cuda_err = [&](const char* what, cudaError_t e) {
         t_shard_msg = std::string(fn) + ": " + what + ": " + cudaGetErrorString(e);
         return sdq::set_error_message(SDQ_ERR_CUDA, t_shard_msg.c_str());
     };
     const ValueFn wait = wait_value_fn();
-    // Every rank has finished permuting out of its buffer from the previous call before
-    // anyone pushes into it again.
+    // The side stream first waits for everything already on the caller's stream (a reader
+    // of the previous result in the symmetric output among it); then one barrier, after
+    // which no rank is still reading its output when the peers start pushing into it.
+    cudaError_t e = cudaEventRecord(c->ev_entry, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->ev_entry, 0);
+    if (e != cudaSuccess) return cuda_err("stream set-up", e);
     ncclResult_t r = side_barrier(c, c->side);
     if (r != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
-    cudaError_t e = cudaEventRecord(c->ev_bar, c->side);
+    // The kernel needs no barrier: the previous call's copy out of this rank's output was
+    // joined into the caller's stream.  The pushes follow the barrier and the counters' reset.
+    e = cudaEventRecord(c->ev_bar, c->side);
     if (e == cudaSuccess) e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = cudaEventRecord(c->ev_start, st);
-    // The pushes follow the barrier (side) and the counters' reset (st).
     for (int p = 0; e == cudaSuccess && p < c->world; ++p) {
         if (p == c->rank) continue;
         e = cudaStreamWaitEvent(c->push[p], c->ev_bar, 0);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0);
     }
     if (e != cudaSuccess) return cuda_err("stream set-up", e);
+    // The kernel writes this rank's block straight into its column block of the output.
     const char* msg = nullptr;
-    e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits,
-                                  sdq::bias_only(bias_local), mine, st,
-                                  &msg, c->counters, (int)tpc, (int)nch, 0);
+    e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits, sdq::bias_only(bias_local),
+                                  out + static_cast<size_t>(c->rank) * n_local, ldy, st, &msg,
+                                  c->counters, (int)tpc, (int)nch, grid_cap);
     if (e != cudaSuccess) {
         if (msg) {
             t_shard_msg = std::string(fn) + ": " + msg;
@@ -294,21 +301,24 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
             if (p != c->rank && (e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0)) != cudaSuccess)
                 return cuda_err("stream wait", e);
     }
+    // Each finished chunk of rows goes, as one 2-D copy, into the same rows and column
+    // block of every peer's output.
+    const size_t pitch = static_cast<size_t>(ldy) * sizeof(uint16_t);
     for (int64_t i = 0; i < nch; ++i) {
         const int64_t t0 = i * tpc, t1 = (i + 1) * tpc < ntt ? (i + 1) * tpc : ntt;
         const int64_t m0 = t0 * bt, m1 = t1 * bt < m ? t1 * bt : m;
         const cuuint32_t target = static_cast<cuuint32_t>((t1 - t0) * nft);
-        const size_t off = static_cast<size_t>(m0) * n_local;
-        const size_t bytes = static_cast<size_t>(m1 - m0) * n_local * sizeof(uint16_t);
+        const size_t off = static_cast<size_t>(m0) * ldy + static_cast<size_t>(c->rank) * n_local;
         for (int p = 0; p < c->world; ++p) {
             if (p == c->rank) continue;
             if (wait != nullptr &&
                 wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->counters + i),
                      target, 0 /* GEQ */) != CUDA_SUCCESS)
                 return cuda_err("stream wait on a chunk count", cudaErrorUnknown);
-            uint16_t* dst = static_cast<uint16_t*>(c->peer_xbuf[p]) + c->rank * block + off;
-            if ((e = cudaMemcpyAsync(dst, mine + off, bytes, cudaMemcpyDeviceToDevice, c->push[p])) !=
-                cudaSuccess)
+            uint16_t* dst = static_cast<uint16_t*>(c->peer_xbuf[p]) + off;
+            if ((e = cudaMemcpy2DAsync(dst, pitch, out + off, pitch, n_local * sizeof(uint16_t),
+                                       static_cast<size_t>(m1 - m0), cudaMemcpyDeviceToDevice,
+                                       c->push[p])) != cudaSuccess)
                 return cuda_err("push to a peer", e);
         }
     }
@@ -318,24 +328,25 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
             (e = cudaStreamWaitEvent(c->side, c->push_done[p], 0)) != cudaSuccess)
             return cuda_err("push join", e);
     }
-    // All pushes into this rank's buffer have landed once every rank has passed here.
+    // This rank's own block is complete once the kernel is (its last chunk's count).
+    if ((e = cudaEventRecord(c->ev_kernel, st)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(c->side, c->ev_kernel, 0)) != cudaSuccess)
+        return cuda_err("stream join", e);
+    // Every push into this rank's output has landed once every rank has passed here.
     if ((r = side_barrier(c, c->side)) != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
-    const int threads = 256;
-    if (n_local % 8 == 0) {
-        const int64_t total = static_cast<int64_t>(c->world) * m * (n_local / 8);
-        int64_t grid = (total + threads - 1) / threads;
+    if (y != out) {
+        const int threads = 256;
+        const bool v8 = (reinterpret_cast<uintptr_t>(y) % 16) == 0 && total % 8 == 0;
+        const int64_t work = v8 ? static_cast<int64_t>(total / 8) : static_cast<int64_t>(total);
+        int64_t grid = (work + threads - 1) / threads;
         if (grid > 4096) grid = 4096;
-        permute_exchange_v8<<<(int)grid, threads, 0, c->side>>>(
-            reinterpret_cast<const uint4*>(xb), reinterpret_cast<const uint4*>(mine),
-            static_cast<uint4*>(y), m, n_local / 8, c->world, c->rank);
-    } else {
-        const int64_t total = static_cast<int64_t>(c->world) * m * n_local;
-        int64_t grid = (total + threads - 1) / threads;
-        if (grid > 4096) grid = 4096;
-        permute_exchange_v1<<<(int)grid, threads, 0, c->side>>>(xb, mine, static_cast<uint16_t*>(y), m,
-                                                                n_local, c->world, c->rank);
+        if (v8)
+            copy_v8<<<(int)grid, threads, 0, c->side>>>(reinterpret_cast<const uint4*>(out),
+                                                         static_cast<uint4*>(y), work);
+        else
+            copy_v1<<<(int)grid, threads, 0, c->side>>>(out, static_cast<uint16_t*>(y), work);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_err("output copy", e);
     }
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_err("permute kernel", e);
     e = cudaEventRecord(c->ev_end, c->side);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->ev_end, 0);
     if (e != cudaSuccess) return cuda_err("stream join", e);
@@ -376,6 +387,8 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
                    cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_bar, cudaEventDisableTiming) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&c->ev_entry, cudaEventDisableTiming) == cudaSuccess &&
+                   cudaEventCreateWithFlags(&c->ev_kernel, cudaEventDisableTiming) == cudaSuccess &&
                    cudaMalloc(reinterpret_cast<void**>(&c->counters), (kMaxChunks + 1) * sizeof(uint32_t)) ==
                        cudaSuccess &&
                    world <= kMaxWorld &&
@@ -388,8 +401,10 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
         if (!okr) {
             cudaGetLastError();
             destroy_push_streams(c);
-            if (c->ev_bar) cudaEventDestroy(c->ev_bar);
-            c->ev_bar = nullptr;
+            for (cudaEvent_t* ev : {&c->ev_bar, &c->ev_entry, &c->ev_kernel}) {
+                if (*ev) cudaEventDestroy(*ev);
+                *ev = nullptr;
+            }
             if (c->handles_dev) cudaFree(c->handles_dev);
             if (c->counters) cudaFree(c->counters);
             if (c->ev_end) cudaEventDestroy(c->ev_end);
@@ -405,6 +420,17 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
     return sdq::set_error_message(SDQ_OK, "");
 }
 
+int sdq_comm_output(void* comm, int64_t m, int64_t n, void** out) {
+    if (!comm || !out || m <= 0 || n <= 0)
+        return sdq::set_error_message(SDQ_ERR_INVALID, "sdq_comm_output: null argument or empty shape");
+    Comm* c = static_cast<Comm*>(comm);
+    const int rc = ensure_exchange_buffer(c, static_cast<size_t>(m) * static_cast<size_t>(n) * sizeof(uint16_t),
+                                          "sdq_comm_output");
+    if (rc != SDQ_OK) return rc;
+    *out = c->xbuf;
+    return sdq::set_error_message(SDQ_OK, "");
+}
+
 int sdq_comm_destroy(void* comm) {
     if (!comm) return sdq::set_error_message(SDQ_OK, "");
     Comm* c = static_cast<Comm*>(comm);
@@ -417,9 +443,14 @@ int sdq_comm_destroy(void* comm) {
         cudaFree(c->counters);
         destroy_push_streams(c);
         cudaEventDestroy(c->ev_bar);
+        cudaEventDestroy(c->ev_entry);
+        cudaEventDestroy(c->ev_kernel);
         cudaEventDestroy(c->ev_end);
         cudaEventDestroy(c->ev_start);
         cudaStreamDestroy(c->side);
+    } else if (c->xbuf) {
+        cudaDeviceSynchronize();
+        cudaFree(c->xbuf);
     }
     ncclResult_t r = ncclCommDestroy(c->nccl);
     delete c;
@@ -442,11 +473,20 @@ static int sharded_impl(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, 
     if (m <= 0 || n_local <= 0)
         return sdq::set_error_message(SDQ_ERR_INVALID,
                                       "sdq_quantized_matmul_sharded: m and n_local must be >= 1");
+    // y inside the communicator's output buffer must fit in it: growing the buffer would
+    // free the memory y points to.
+    const uintptr_t yb = reinterpret_cast<uintptr_t>(y), xb = reinterpret_cast<uintptr_t>(c->xbuf);
+    if (y && c->xbuf && yb >= xb && yb < xb + c->xbuf_cap &&
+        yb + static_cast<size_t>(m) * n_local * c->world * sizeof(uint16_t) > xb + c->xbuf_cap)
+        return sdq::set_error_message(SDQ_ERR_INVALID,
+                                      "sdq_quantized_matmul_sharded: y lies in the communicator's output "
+                                      "buffer, which is smaller than the output; call sdq_comm_output "
+                                      "with this shape first");
     const size_t chunk = static_cast<size_t>(m) * static_cast<size_t>(n_local);
     uint16_t* mine = static_cast<uint16_t*>(y_shards) + static_cast<size_t>(c->rank) * chunk;
     if (may_overlap && c->world > 1 && y != nullptr && c->side != nullptr && m > 8) {
         const int rc = sharded_overlapped(c, x, x_dtype, m, k, wq, scales, biases, sb_dtype, n_local,
-                                          group_size, bits, bias_local, y_shards, y, y_dtype, stream);
+                                          group_size, bits, bias_local, y, y_dtype, stream);
         if (rc != kNotOverlapped) return rc;
     }
     int rc = sdq_quantized_matmul(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n_local, 1,

@@ -229,10 +229,29 @@ class Comm:
         check(lib().sdq_comm_unique_id(buf))
         return bytes(buf)
 
+    def output(self, m: int, n: int) -> torch.Tensor:
+        """The communicator's output buffer as an [m, n] bf16 tensor (``sdq_comm_output``):
+        passed as ``out`` of :func:`quantized_matmul_sharded`, the result is assembled there
+        with no final copy.  Collective (same m, n on every rank).  The tensor does not own the
+        memory: it is valid until a larger output is asked for or the communicator is destroyed,
+        and every sharded call overwrites it."""
+        p = ctypes.c_void_p()
+        check(lib().sdq_comm_output(self.handle, m, n, ctypes.byref(p)))
+        return torch.as_tensor(_DeviceMemory(p.value, (m, n)),
+                               device=torch.device("cuda", torch.cuda.current_device())).view(torch.bfloat16)
+
     def destroy(self) -> None:
         if self.handle:
             check(lib().sdq_comm_destroy(self.handle))
             self.handle = None
+
+
+class _DeviceMemory:
+    """Library-owned device memory seen through the CUDA array interface (int16 elements)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
 
 
 def shard_rows(n_total: int, world: int, rank: int) -> tuple[int, int]:

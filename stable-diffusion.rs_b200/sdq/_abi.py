@@ -40,6 +40,7 @@ SIGNATURES = {
     "sdq_comm_unique_id": (_i32, [_p]),
     "sdq_comm_init": (_i32, [_p, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)]),
     "sdq_comm_destroy": (_i32, [_p]),
+    "sdq_comm_output": (_i32, [_p, _i64, _i64, ctypes.POINTER(ctypes.c_void_p)]),
     "sdq_quantized_matmul_sharded": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32,
                                             _p, _p, _p, _i32, _p, _p]),
     "sdq_quantized_matmul_sharded_static": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32,

@@ -62,7 +62,7 @@ def _free_port() -> int:
         return sk.getsockname()[1]
 
 
-def _rank_main(rank, world, port, m, k, n, bits, q):
+def _rank_main(rank, world, port, m, k, n, bits, q, into_comm_output=False):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -78,12 +78,17 @@ def _rank_main(rank, world, port, m, k, n, bits, q):
             x = _x(m, k, "cuda")
             full = sdq.quantized_matmul(x, wq, s, b, 64, bits)
             lo, hi = sdq.shard_rows(n, world, rank)
-            out, _ = sdq.quantized_matmul_sharded(x, wq[lo:hi].contiguous(), s[lo:hi].contiguous(),
-                                                  b[lo:hi].contiguous(), comm, 64, bits)
-            torch.cuda.synchronize()
-            sdq.device_status()
-            same = torch.equal(out.view(torch.int16), full.view(torch.int16))
-            rel = float((out.float() - full.float()).abs().max() / full.float().abs().max())
+            args = (x, wq[lo:hi].contiguous(), s[lo:hi].contiguous(), b[lo:hi].contiguous(), comm, 64, bits)
+            target = comm.output(m, n) if into_comm_output else None
+            same, rel = True, 0.0
+            for call in range(2):       # the second call reuses the exchange state
+                out, _ = sdq.quantized_matmul_sharded(*args, out=target)
+                torch.cuda.synchronize()
+                sdq.device_status()
+                same = same and torch.equal(out.view(torch.int16), full.view(torch.int16))
+                rel = max(rel, float((out.float() - full.float()).abs().max() / full.float().abs().max()))
+                if target is not None:
+                    assert out.data_ptr() == target.data_ptr()
             q.put((rank, same, rel))
         finally:
             comm.destroy()
@@ -93,15 +98,19 @@ def _rank_main(rank, world, port, m, k, n, bits, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("into_comm_output", [False, True], ids=["caller_y", "comm_output"])
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("m", [4, 256, 1000])
-def test_two_gpu_sharded_linear_reassembles_the_full_product(bits, m):
+def test_two_gpu_sharded_linear_reassembles_the_full_product(bits, m, into_comm_output):
+    """m = 4: the plain path (kernel, ncclAllGather, permute); m = 256 / 1000: the overlapped
+    path, its result assembled in the communicator's output and copied to the caller's y, or
+    left in place when y is that output."""
     import torch.multiprocessing as mp
     world, k, n = 2, 512, 1024
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, k, n, bits, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, k, n, bits, q, into_comm_output))
              for r in range(world)]
     for p in procs:
         p.start()
