@@ -151,6 +151,45 @@ int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, i
  */
 size_t sdq_resident_bytes(int64_t n, int64_t k, int group_size, int bits, int sb_bytes);
 
+/* GGML block types of GGUF tensors (the file's type ids, crates/sd-tensor/src/mlx_gguf.rs:
+ * 61-78): the set the reference's checkpoints use. */
+#define SDQ_GGML_F32 0
+#define SDQ_GGML_F16 1
+#define SDQ_GGML_Q4_0 2
+#define SDQ_GGML_Q8_0 8
+#define SDQ_GGML_Q4_K 12
+#define SDQ_GGML_Q5_K 13
+#define SDQ_GGML_Q6_K 14
+#define SDQ_GGML_BF16 30
+
+/*
+ * Bytes of GGUF data for `elems` values of block type ggml_type, or 0 when the type is
+ * not one of SDQ_GGML_* or elems is not a whole number of blocks (mlx_gguf.rs:80-93,
+ * 237-244).
+ */
+size_t sdq_gguf_bytes(int ggml_type, int64_t elems);
+
+/*
+ * Quantise a GGUF tensor's raw data (device memory, 4-byte aligned, sdq_gguf_bytes(type,
+ * n*k) bytes; the tensor's row-major [n, k]) straight into wq / scales / biases, as
+ * sdq_quantize would quantise its f32 dequantisation -- bit for bit -- without
+ * materialising it.  Replaces, per tensor, the reference's Gguf::dequantize followed by
+ * QuantizedArray::quantize in quantized::from_gguf (crates/sd-models/src/mlx/
+ * quantized.rs:180-211; mlx_gguf.rs:235-435).  k must be a multiple of 64 and of the
+ * type's block size; the other arguments are sdq_quantize's.
+ */
+int sdq_gguf_quantize(const void* raw, int ggml_type, int64_t n, int64_t k, int group_size, int bits,
+                      uint32_t* wq, void* scales, void* biases, sdq_dtype sb_dtype, void* stream);
+
+/*
+ * Dequantise a GGUF tensor's raw data (device memory, as above) to `count` values of
+ * out_dtype (SDQ_F32: the reference's f32 values exactly; SDQ_BF16: those rounded to
+ * nearest even).  Replaces Gguf::dequantize (mlx_gguf.rs:235-283) for the tensors that stay
+ * dense.
+ */
+int sdq_gguf_dequantize(const void* raw, int ggml_type, int64_t count, void* out, sdq_dtype out_dtype,
+                        void* stream);
+
 /*
  * Read back and clear the device-side status word that the kernels set when a
  * bounded wait gives up.  Synchronises `stream`.  Returns SDQ_OK or

@@ -160,6 +160,87 @@ def epilogue(acc: np.ndarray, bias_bf16=None, act: int = ACT_NONE, gate_bf16=Non
     return a
 
 
+# ---------------------------------------------------------------- GGUF block formats
+# The reference's host dequantisation of GGUF tensors (crates/sd-tensor/src/mlx_gguf.rs:235-435),
+# restated in NumPy float32 so that every product and difference rounds as the Rust code's does.
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_BF16 = 0, 1, 2, 8, 12, 13, 14, 30
+GGML_BLOCKS = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_BF16: (1, 2), GGML_Q4_0: (32, 18), GGML_Q8_0: (32, 34),
+               GGML_Q4_K: (256, 144), GGML_Q5_K: (256, 176), GGML_Q6_K: (256, 210)}
+
+
+def _f16(raw2: np.ndarray) -> np.ndarray:
+    """Little-end f16 bytes [..., 2] -> float32 (exact; mlx_gguf.rs:298-318)."""
+    return np.ascontiguousarray(raw2).view("<f2")[..., 0].astype(np.float32)
+
+
+def _scale_min_k4(q: np.ndarray):
+    """[blocks, 12] packed bytes -> (scales, mins) [blocks, 8] (mlx_gguf.rs:346-360)."""
+    q = q.astype(np.int32)
+    sc = np.empty((q.shape[0], 8), np.int32)
+    mn = np.empty_like(sc)
+    sc[:, :4] = q[:, 0:4] & 63
+    mn[:, :4] = q[:, 4:8] & 63
+    sc[:, 4:] = (q[:, 8:12] & 0x0F) | ((q[:, 0:4] >> 6) << 4)
+    mn[:, 4:] = (q[:, 8:12] >> 4) | ((q[:, 4:8] >> 6) << 4)
+    return sc, mn
+
+
+def gguf_dequantize(raw: np.ndarray, ggml_type: int, count: int) -> np.ndarray:
+    """``Gguf::dequantize`` (mlx_gguf.rs:235-283): `count` values of a GGUF tensor as float32."""
+    per, nbytes = GGML_BLOCKS[ggml_type]
+    if count % per != 0:
+        raise ValueError(f"oracle.gguf_dequantize: {count} values are not whole blocks of {per}")
+    blocks = count // per
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)[: blocks * nbytes].reshape(blocks, nbytes)
+    f32 = np.float32
+    if ggml_type == GGML_F32:
+        return raw.reshape(-1).view("<f4").astype(f32)
+    if ggml_type == GGML_F16:
+        return raw.reshape(-1).view("<f2").astype(f32)
+    if ggml_type == GGML_BF16:
+        return (raw.reshape(-1).view("<u2").astype(np.uint32) << 16).view(f32)
+    if ggml_type == GGML_Q4_0:                       # mlx_gguf.rs:325-335
+        d = _f16(raw[:, 0:2])[:, None]
+        qs = raw[:, 2:18].astype(np.int32)
+        q = np.concatenate([(qs & 0x0F) - 8, (qs >> 4) - 8], axis=1).astype(f32)
+        return (d * q).reshape(-1)
+    if ggml_type == GGML_Q8_0:                       # mlx_gguf.rs:337-344
+        d = _f16(raw[:, 0:2])[:, None]
+        return (d * raw[:, 2:34].view(np.int8).astype(f32)).reshape(-1)
+    if ggml_type in (GGML_Q4_K, GGML_Q5_K):          # mlx_gguf.rs:362-410
+        d = _f16(raw[:, 0:2])[:, None]
+        dmin = _f16(raw[:, 2:4])[:, None]
+        sc, mn = _scale_min_k4(raw[:, 4:16])
+        d1 = (d * sc.astype(f32))                    # [blocks, 8]
+        m1 = (dmin * mn.astype(f32))
+        qs = raw[:, 16:144] if ggml_type == GGML_Q4_K else raw[:, 48:176]
+        qs = qs.astype(np.int32).reshape(blocks, 4, 32)
+        q = np.empty((blocks, 8, 32), np.int32)
+        q[:, 0::2] = qs & 0x0F
+        q[:, 1::2] = qs >> 4
+        if ggml_type == GGML_Q5_K:
+            qh = raw[:, 16:48].astype(np.int32)      # [blocks, 32]
+            for j in range(8):
+                q[:, j] |= ((qh >> j) & 1) << 4
+        return (d1[:, :, None] * q.astype(f32) - m1[:, :, None]).reshape(-1)
+    if ggml_type == GGML_Q6_K:                       # mlx_gguf.rs:412-435
+        ql = raw[:, 0:128].astype(np.int32).reshape(blocks, 2, 64)
+        qh = raw[:, 128:192].astype(np.int32).reshape(blocks, 2, 32)
+        sc = raw[:, 192:208].view(np.int8).astype(f32).reshape(blocks, 2, 8)
+        d = _f16(raw[:, 208:210])[:, None, None]
+        out = np.empty((blocks, 2, 4, 32), f32)
+        parts = [((ql[:, :, :32] & 0x0F) | ((qh & 3) << 4)) - 32,
+                 ((ql[:, :, 32:] & 0x0F) | (((qh >> 2) & 3) << 4)) - 32,
+                 ((ql[:, :, :32] >> 4) | (((qh >> 4) & 3) << 4)) - 32,
+                 ((ql[:, :, 32:] >> 4) | (((qh >> 6) & 3) << 4)) - 32]
+        for quad, q in enumerate(parts):
+            # sc[is + 2 quad] with is = l / 16: scales 2 quad and 2 quad + 1 for l < 16 / >= 16
+            s = np.repeat(sc[:, :, 2 * quad:2 * quad + 2], 16, axis=2)
+            out[:, :, quad, :] = (d * s) * q.astype(f32)
+        return out.reshape(-1)
+    raise ValueError(f"oracle.gguf_dequantize: unknown GGML type {ggml_type}")
+
+
 def resident_bytes(n: int, k: int, bits: int, group_size: int = GROUP) -> int:
     return int(lib().oracle_resident_bytes(n, k, group_size, bits))
 

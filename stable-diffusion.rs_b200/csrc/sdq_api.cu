@@ -264,6 +264,63 @@ int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, i
     return run_qmm(x, m, k, wq, scales, biases, n, bits, epi, y, stream, fn);
 }
 
+size_t sdq_gguf_bytes(int ggml_type, int64_t elems) {
+    int values = 0, bytes = 0;
+    if (!sdq::gguf_block(ggml_type, values, bytes) || elems <= 0 || elems % values != 0) return 0;
+    return static_cast<size_t>(elems / values) * static_cast<size_t>(bytes);
+}
+
+int sdq_gguf_quantize(const void* raw, int ggml_type, int64_t n, int64_t k, int group_size, int bits,
+                      uint32_t* wq, void* scales, void* biases, sdq_dtype sb_dtype, void* stream) {
+    const char* fn = "sdq_gguf_quantize";
+    int rc;
+    if ((rc = check_qparams(group_size, bits, "affine", fn))) return rc;
+    if ((rc = check_nk(n, k, fn))) return rc;
+    int values = 0, bytes = 0;
+    if (!sdq::gguf_block(ggml_type, values, bytes))
+        return fail(SDQ_ERR_UNSUPPORTED,
+                    "%s: GGML type %d is not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K)", fn,
+                    ggml_type);
+    if (k % values != 0)
+        return fail(SDQ_ERR_INVALID, "%s: rows of %lld values are not whole blocks of %d", fn, (long long)k,
+                    values);
+    if (!raw || !wq || !scales || !biases)
+        return fail(SDQ_ERR_INVALID, "%s: raw, wq, scales and biases must be non-null", fn);
+    if (sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 only (dtype %d)", fn, (int)sb_dtype);
+    if (!aligned(raw, 4) || !aligned(wq, 4) || !aligned(scales, 2) || !aligned(biases, 2))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (raw and wq need 4 bytes)", fn);
+    if ((rc = check_device())) return rc;
+    cudaError_t e = launch_gguf_quantize(raw, ggml_type, n, k, bits, wq, scales, biases,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_gguf_quantize: kernel launch", e);
+    return ok();
+}
+
+int sdq_gguf_dequantize(const void* raw, int ggml_type, int64_t count, void* out, sdq_dtype out_dtype,
+                        void* stream) {
+    const char* fn = "sdq_gguf_dequantize";
+    int values = 0, bytes = 0;
+    if (!sdq::gguf_block(ggml_type, values, bytes))
+        return fail(SDQ_ERR_UNSUPPORTED,
+                    "%s: GGML type %d is not supported (F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K)", fn,
+                    ggml_type);
+    if (count <= 0 || count % values != 0)
+        return fail(SDQ_ERR_INVALID, "%s: %lld values are not a whole number of blocks of %d", fn,
+                    (long long)count, values);
+    if (!raw || !out) return fail(SDQ_ERR_INVALID, "%s: raw and out must be non-null", fn);
+    if (out_dtype != SDQ_F32 && out_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: out must be f32 or bf16 (dtype %d)", fn, (int)out_dtype);
+    if (!aligned(raw, 4) || !aligned(out, out_dtype == SDQ_F32 ? 4 : 2))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (raw needs 4 bytes)", fn);
+    int rc;
+    if ((rc = check_device())) return rc;
+    cudaError_t e = launch_gguf_dequantize(raw, ggml_type, count, out, out_dtype == SDQ_F32,
+                                           static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_gguf_dequantize: kernel launch", e);
+    return ok();
+}
+
 int sdq_device_status(void* stream) {
     int rc;
     if ((rc = check_device())) return rc;

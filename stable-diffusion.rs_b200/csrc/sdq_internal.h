@@ -73,6 +73,14 @@ cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, 
                        const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y,
                        cudaStream_t st, const char** msg, bool* taken);
 
+// GGUF block types (sdq_gguf.cu): values and bytes per block (0 for an unknown type), and
+// the fused dequantise-quantise / the dense dequantise kernels.
+int gguf_block(int type, int& values, int& bytes);
+cudaError_t launch_gguf_quantize(const void* raw, int type, int64_t n, int64_t k, int bits, uint32_t* wq,
+                                 void* scales, void* biases, cudaStream_t st);
+cudaError_t launch_gguf_dequantize(const void* raw, int type, int64_t count, void* out, bool out_f32,
+                                   cudaStream_t st);
+
 // Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st);
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st);

@@ -20,7 +20,7 @@ from ._abi import (SDQ_BF16, SDQ_ERR_CUDA, SDQ_ERR_INVALID, SDQ_ERR_NCCL, SDQ_ER
 
 __all__ = [
     "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "quantized_matmul_epilogue",
-    "resident_bytes", "ACT_NONE", "ACT_GELU_TANH", "ACT_SILU",
+    "gguf_quantize", "gguf_dequantize", "resident_bytes", "ACT_NONE", "ACT_GELU_TANH", "ACT_SILU",
     "device_status", "Comm", "quantized_matmul_sharded", "shard_rows", "unshard", "GROUP_SIZE", "MODE",
     "SDQ_OK", "SDQ_ERR_INVALID", "SDQ_ERR_UNSUPPORTED", "SDQ_ERR_CUDA", "SDQ_ERR_TIMEOUT",
     "SDQ_ERR_NCCL",
@@ -146,6 +146,38 @@ def quantized_matmul_epilogue(x: torch.Tensor, wq, scales, biases, group_size: i
     check(lib().sdq_quantized_matmul_epilogue(
         _ptr(x), _dt(x), m, k, _ptr(wq), _ptr(scales), _ptr(biases), _dt(scales), n, group_size, bits,
         _ptr(bias), _ACTS[act], _ptr(gate), _ptr(residual), _ptr(out), _dt(out), _stream(stream)))
+    return out
+
+
+def gguf_quantize(raw: torch.Tensor, ggml_type: int, n: int, k: int, bits: int = 4,
+                  group_size: int = GROUP_SIZE, stream=None):
+    """A GGUF tensor's raw block bytes (uint8 device tensor) -> (wq, scales, biases) of its
+    row-major [n, k], bit-identical to quantising its f32 dequantisation (``sdq_gguf_quantize``)."""
+    _need_cuda(raw)
+    wq = torch.empty((n, k * bits // 32), device=raw.device, dtype=torch.int32)
+    s = torch.empty((n, k // GROUP_SIZE), device=raw.device, dtype=torch.bfloat16)
+    b = torch.empty_like(s)
+    need = int(lib().sdq_gguf_bytes(ggml_type, n * k))
+    if need and raw.numel() * raw.element_size() < need:
+        raise SdqError(SDQ_ERR_INVALID, f"gguf_quantize: {raw.numel()} bytes, the tensor needs {need}")
+    check(lib().sdq_gguf_quantize(_ptr(raw), ggml_type, n, k, group_size, bits, _ptr(wq), _ptr(s), _ptr(b),
+                                  SDQ_BF16, _stream(stream)))
+    return wq, s, b
+
+
+def gguf_dequantize(raw: torch.Tensor, ggml_type: int, shape, out_dtype=torch.float32,
+                    stream=None) -> torch.Tensor:
+    """A GGUF tensor's raw block bytes (uint8 device tensor) -> its values, f32 exactly as the
+    reference's host dequantisation gives them, or bf16 (``sdq_gguf_dequantize``)."""
+    _need_cuda(raw)
+    count = 1
+    for d in shape:
+        count *= d
+    need = int(lib().sdq_gguf_bytes(ggml_type, count))
+    if need and raw.numel() * raw.element_size() < need:
+        raise SdqError(SDQ_ERR_INVALID, f"gguf_dequantize: {raw.numel()} bytes, the tensor needs {need}")
+    out = torch.empty(tuple(shape), device=raw.device, dtype=out_dtype)
+    check(lib().sdq_gguf_dequantize(_ptr(raw), ggml_type, count, _ptr(out), _dt(out), _stream(stream)))
     return out
 
 

@@ -36,6 +36,9 @@ SIGNATURES = {
     "sdq_quantized_matmul_epilogue": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32,
                                              _p, _i32, _p, _p, _p, _i32, _p]),
     "sdq_resident_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32]),
+    "sdq_gguf_bytes": (_sz, [_i32, _i64]),
+    "sdq_gguf_quantize": (_i32, [_p, _i32, _i64, _i64, _i32, _i32, _p, _p, _p, _i32, _p]),
+    "sdq_gguf_dequantize": (_i32, [_p, _i32, _i64, _p, _i32, _p]),
     "sdq_device_status": (_i32, [_p]),
     "sdq_comm_unique_id": (_i32, [_p]),
     "sdq_comm_init": (_i32, [_p, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)]),

@@ -119,6 +119,49 @@ def from_dense_with(w: Mapping[str, torch.Tensor], bits_for: Callable[[str], int
     return QuantizedWeights(quantized, dense)
 
 
+def from_gguf(path: str, bits: int, device=None, stream=None) -> QuantizedWeights:
+    """Load a GGUF checkpoint, quantising the large weights as they are read
+    (quantized.rs:180-211).  One tensor at a time: its raw block bytes are copied to the
+    device and either quantised there straight from the block format (``sdq.gguf_quantize``)
+    or dequantised to a dense f32 tensor; nothing else of the file is held meanwhile."""
+    return _load_gguf(path, bits, None, device, stream)
+
+
+def from_gguf_renamed(path: str, bits: int, rename: Callable[[str], Optional[str]], device=None,
+                      stream=None) -> QuantizedWeights:
+    """``from_gguf`` with file names translated by ``rename`` (None drops a tensor),
+    quantized.rs:221-255."""
+    return _load_gguf(path, bits, rename, device, stream)
+
+
+def _load_gguf(path, bits, rename, device, stream) -> QuantizedWeights:
+    from . import gguf as G
+    from . import gguf_dequantize, gguf_quantize
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    g = G.Gguf(path)
+    quantized: Dict[str, QuantizedArray] = {}
+    dense: Weights = {}
+    policy = mixed(bits)
+    for info in g.tensors:
+        name = info.name if rename is None else rename(info.name)
+        if name is None:
+            continue
+        raw = torch.from_numpy(g.raw(info)).to(dev)         # the peak: one tensor's blocks
+        want = policy(name)
+        if want >= 2 and quantizable(info.shape):
+            n, k = info.shape
+            wq, s, b = gguf_quantize(raw, info.kind, n, k, want, GROUP_SIZE, stream)
+            quantized[name] = QuantizedArray(wq, s, b, GROUP_SIZE, want)
+        else:
+            dense[name] = gguf_dequantize(raw, info.kind, info.shape, torch.float32, stream)
+        del raw
+    if not quantized and not dense:
+        raise SdqError(SDQ_ERR_INVALID, f"gguf: {path} carries no tensors"
+                       + ("" if rename is None else " this model recognises"))
+    return QuantizedWeights(quantized, dense)
+
+
 def dense_linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None) -> torch.Tensor:
     """The reference's dense ``x @ w.T + b`` (crates/sd-models/src/mlx/mod.rs:182-189)."""
     y = torch.matmul(x, w.t().to(x.dtype))
