@@ -112,7 +112,9 @@ size_t smem_bytes(int64_t k) {
     return b;
 }
 
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
+// FUSED: the output stage applies gate / residual / activation (EpiArgs::fused); the plain
+// instantiation adds the bias only and carries none of that code.
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED>
 __global__ void __launch_bounds__(tc_threads(BITS), 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
@@ -381,19 +383,18 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         // accumulator is waited on (the copy overlaps the tile's main loop) and the output
         // is formed in place there; otherwise each thread loads its residual elements.
         static_assert(kEpiGroups == 1, "one residual barrier serves one epilogue group");
-        const bool fused = epi.gate != nullptr || epi.resid != nullptr || epi.act != SDQ_ACT_NONE;
         int tc = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
             const int tt = tile / nft, ft = tile - tt * nft;
             const int f = ft * C::BF + fl;
             const float badd = (epi.bias != nullptr && f < N) ? bf16_bits_to_f32(epi.bias[f]) : 0.f;
-            const float gmul = (epi.gate != nullptr && f < N) ? bf16_bits_to_f32(epi.gate[f]) : 1.f;
+            const float gmul = (FUSED && epi.gate != nullptr && f < N) ? bf16_bits_to_f32(epi.gate[f]) : 1.f;
             // The staging chunks of this group must have been read by the previous
             // tile's stores before they are overwritten.
             if (leader && y_tma) bulk_wait_group_read0();
             named_barrier_sync(1 + e, 128);
             bool ok = true;
-            if (r_tma) {
+            if (FUSED && r_tma) {
                 if (leader) {
                     uint32_t bytes = 0;
                     for (int c = e; c < NCH; c += kEpiGroups)
@@ -420,7 +421,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                         __syncwarp();
                         tmem_ld16(tmem + lane_base + C::D_COL + (uint32_t)(CW * c + 16 * h), v);
                         tc_wait_ld();
-                        if (!fused) {
+                        if constexpr (!FUSED) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 yrow[(16 * h + j) * C::BF] =
@@ -501,7 +502,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
 constexpr size_t kMaxSmem = kQmvMaxSmem;
 
 
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
                         cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
@@ -561,7 +562,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     // The residual ([m, n], contiguous) is copied in by TMA under the same conditions.
     CUtensorMap tmR;
     std::memset(&tmR, 0, sizeof(tmR));
-    const bool r_tma = y_tma && n % 8 == 0 && epi.resid != nullptr &&
+    const bool r_tma = FUSED && y_tma && n % 8 == 0 && epi.resid != nullptr &&
                        (reinterpret_cast<uintptr_t>(epi.resid) % 16) == 0;
     if (r_tma) {
         cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
@@ -583,7 +584,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     if (e != cudaSuccess) return e;
     static bool configured[64] = {};
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES>,
+        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -591,7 +592,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
     const int grid = (int)(tiles < cap ? tiles : cap);
-    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES><<<grid, tc_threads(BITS), smem, st>>>(
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
         ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
@@ -628,6 +629,18 @@ int choose_tile(int64_t m, int64_t k, int64_t n, int grid_cap) {
     return bt;
 }
 
+// The plain or the fused instantiation of a configuration, as the output stage asks.
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
+cudaError_t launch_tc_f(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
+                        const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
+                        cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
+    if (epi.fused())
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
+                                                             msg, sig, grid_cap);
+    return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
+                                                          msg, sig, grid_cap);
+}
+
 template <int BITS>
 cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                            const void* scales, const void* biases, int64_t n, const EpiArgs& epi,
@@ -637,13 +650,13 @@ cudaError_t launch_tc_bits(const void* x, int64_t m, int64_t k, const uint32_t* 
     constexpr int SWs = BITS == 4 ? 16 : 12;
     constexpr int SWL = BITS == 4 ? 8 : 4;
     switch (choose_tile<BITS>(m, k, n, grid_cap)) {
-        case 0: return launch_tc_t<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        case 16: return launch_tc_t<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        case 64: return launch_tc_t<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        case 128: return launch_tc_t<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        case 176: return launch_tc_t<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        case 240: return launch_tc_t<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
-        default: return launch_tc_t<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 0: return launch_tc_f<BITS, 16, 1, SWs, 14, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 16: return launch_tc_f<BITS, 16, 8, 12, 14, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 64: return launch_tc_f<BITS, 64, 8, 12, 12, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 128: return launch_tc_f<BITS, 128, 6, 8, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 176: return launch_tc_f<BITS, 176, 5, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        case 240: return launch_tc_f<BITS, 240, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+        default: return launch_tc_f<BITS, 256, 4, SWL, 8, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
     }
 }
 
