@@ -43,6 +43,8 @@ WORKLOADS = {
     "cfg3": (8, 3072, 18432, 4, 0.02, "gbs"),
     "cfg5": (16384, 3072, 12288, 4, 0.02, "tflops"),
 }
+# One SeededRng seed per config (the draw of X then W).
+SEEDS = {"cfg1": 1, "cfg2": 2, "cfg3": 3, "cfg5": 5}
 DESCR = {
     "cfg1": "config 1: X bf16[1024,3072] . W[3072,3072]^T, W4 g64",
     "cfg2": "config 2: X bf16[4096,12288] . W[3072,12288]^T, W8 g64 (Flux MLP down-proj at 1024^2)",
@@ -506,13 +508,15 @@ def main():
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
 
-    # ---- data: X replicated, this rank's W shard (rows rank*n .. rank*n + n of a [world*n, k] W)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    gx = torch.Generator(device=dev).manual_seed(999)
-    x = torch.randn(m, k, device=dev, generator=gx).to(torch.bfloat16)
-    w = torch.randn(n, k, device=dev, generator=g) * sig
-    wq, s, b = sdq.quantize(w, 64, bits)
-    del w
+    # ---- data: the reference's documented draw (SeededRng, one seed per config): X first, then
+    # the whole [world*n, k] W, each N(0, 1) scaled by sigma; X rounded to bf16, W kept f32 and
+    # quantised by the library.  Every rank draws the same sequence and keeps its W rows
+    # rank*n .. rank*n + n.
+    vals = sdq.seeded_normals(SEEDS[wl], m * k + world * n * k, device=dev)
+    x = (vals[: m * k] * 1.0).view(m, k).to(torch.bfloat16)
+    w = (vals[m * k + rank * n * k: m * k + (rank + 1) * n * k] * sig).view(n, k)
+    wq, s, b = sdq.quantize(w.contiguous(), 64, bits)
+    del w, vals
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     # The timed steps rotate over R copies of the inputs (X, packed W, scales, biases, Y) that
     # together exceed twice the L2, so that no step finds its inputs in L2 and the steps can
@@ -662,7 +666,7 @@ def main():
             "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded torch normal; weights quantised by libsdq)",
+            "data": "synthetic (SeededRng: splitmix64 + Box-Muller, the reference's documented draw; X then W; W quantised by libsdq)",
             "config": {"workload": wl, "descr": DESCR[wl], "M": m, "K": k, "N_per_rank": n, "bits": bits,
                        "group_size": 64, "global_N": n * world,
                        "parallelism": "single GPU" if world == 1 else

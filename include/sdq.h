@@ -191,6 +191,14 @@ int sdq_gguf_dequantize(const void* raw, int ggml_type, int64_t count, void* out
                         void* stream);
 
 /*
+ * `count` f32 standard normals of SeededRng::new(seed).normals(count) (crates/sd-tensor/src/
+ * lib.rs:104-145: splitmix64, Box-Muller in f64, cos then sin), into device memory `out`:
+ * the reference's documented draw for synthetic inputs.  Not on the quantised path; the
+ * benchmark draws its inputs with it.
+ */
+int sdq_seeded_normals(uint64_t seed, int64_t count, float* out, void* stream);
+
+/*
  * Read back and clear the device-side status word that the kernels set when a
  * bounded wait gives up.  Synchronises `stream`.  Returns SDQ_OK or
  * SDQ_ERR_TIMEOUT (with a message naming the wait).  No counterpart in the

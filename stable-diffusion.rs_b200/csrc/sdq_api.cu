@@ -321,6 +321,18 @@ int sdq_gguf_dequantize(const void* raw, int ggml_type, int64_t count, void* out
     return ok();
 }
 
+int sdq_seeded_normals(uint64_t seed, int64_t count, float* out, void* stream) {
+    if (count < 0 || (count > 0 && !out))
+        return fail(SDQ_ERR_INVALID, "sdq_seeded_normals: need count >= 0 and a non-null out");
+    if (!aligned(out, 4)) return fail(SDQ_ERR_INVALID, "sdq_seeded_normals: misaligned out");
+    if (count == 0) return ok();
+    int rc;
+    if ((rc = check_device())) return rc;
+    cudaError_t e = launch_seeded_normals(seed, count, out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_seeded_normals: kernel launch", e);
+    return ok();
+}
+
 int sdq_device_status(void* stream) {
     int rc;
     if ((rc = check_device())) return rc;

@@ -81,6 +81,9 @@ cudaError_t launch_gguf_quantize(const void* raw, int type, int64_t n, int64_t k
 cudaError_t launch_gguf_dequantize(const void* raw, int type, int64_t count, void* out, bool out_f32,
                                    cudaStream_t st);
 
+// SeededRng::normals (sdq_rng.cu).
+cudaError_t launch_seeded_normals(uint64_t seed, int64_t count, float* out, cudaStream_t st);
+
 // Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st);
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st);

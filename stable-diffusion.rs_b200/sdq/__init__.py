@@ -20,7 +20,7 @@ from ._abi import (SDQ_BF16, SDQ_ERR_CUDA, SDQ_ERR_INVALID, SDQ_ERR_NCCL, SDQ_ER
 
 __all__ = [
     "SdqError", "QuantizedArray", "quantize", "dequantize", "quantized_matmul", "quantized_matmul_epilogue",
-    "gguf_quantize", "gguf_dequantize", "resident_bytes", "ACT_NONE", "ACT_GELU_TANH", "ACT_SILU",
+    "gguf_quantize", "gguf_dequantize", "seeded_normals", "resident_bytes", "ACT_NONE", "ACT_GELU_TANH", "ACT_SILU",
     "device_status", "Comm", "quantized_matmul_sharded", "shard_rows", "unshard", "GROUP_SIZE", "MODE",
     "SDQ_OK", "SDQ_ERR_INVALID", "SDQ_ERR_UNSUPPORTED", "SDQ_ERR_CUDA", "SDQ_ERR_TIMEOUT",
     "SDQ_ERR_NCCL",
@@ -178,6 +178,15 @@ def gguf_dequantize(raw: torch.Tensor, ggml_type: int, shape, out_dtype=torch.fl
         raise SdqError(SDQ_ERR_INVALID, f"gguf_dequantize: {raw.numel()} bytes, the tensor needs {need}")
     out = torch.empty(tuple(shape), device=raw.device, dtype=out_dtype)
     check(lib().sdq_gguf_dequantize(_ptr(raw), ggml_type, count, _ptr(out), _dt(out), _stream(stream)))
+    return out
+
+
+def seeded_normals(seed: int, count: int, device=None, stream=None) -> torch.Tensor:
+    """``SeededRng::new(seed).normals(count)`` (crates/sd-tensor/src/lib.rs:104-145) on the
+    device, as f32: the reference's documented draw for synthetic inputs."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out = torch.empty(count, device=dev, dtype=torch.float32)
+    check(lib().sdq_seeded_normals(ctypes.c_uint64(seed), count, _ptr(out), _stream(stream)))
     return out
 
 

@@ -37,6 +37,7 @@ SIGNATURES = {
                                              _p, _i32, _p, _p, _p, _i32, _p]),
     "sdq_resident_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32]),
     "sdq_gguf_bytes": (_sz, [_i32, _i64]),
+    "sdq_seeded_normals": (_i32, [ctypes.c_uint64, _i64, _p, _p]),
     "sdq_gguf_quantize": (_i32, [_p, _i32, _i64, _i64, _i32, _i32, _p, _p, _p, _i32, _p]),
     "sdq_gguf_dequantize": (_i32, [_p, _i32, _i64, _p, _i32, _p]),
     "sdq_device_status": (_i32, [_p]),

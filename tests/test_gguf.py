@@ -213,3 +213,19 @@ def test_from_gguf_quantises_by_the_reference_policy(tmp_path):
     with pytest.raises(SdqError) as e:
         Q.from_gguf_renamed(path, 4, lambda n: None)
     assert "carries no tensors this model recognises" in str(e.value)
+
+
+# ---------------------------------------------------------------- the synthetic-input draw
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not gpu_available(), reason="needs an sm_100 device")
+@pytest.mark.parametrize("seed,count", [(0, 1), (7, 1001), (2, 1 << 20)])
+def test_gpu_seeded_normals_are_the_reference_draw(seed, count):
+    """sdq_seeded_normals against the oracle's SeededRng (lib.rs:104-145).  The f64 log / sincos
+    of the device and of the host libm may differ in the last f64 place, which moves an f32
+    result by one unit in the rare case it lands on a rounding boundary."""
+    import sdq
+    got = sdq.seeded_normals(seed, count).cpu().numpy()
+    want = O.seeded_normals(seed, count)
+    diff = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+    assert diff.max() <= 1 and np.count_nonzero(diff) <= max(1, count // 100000)
