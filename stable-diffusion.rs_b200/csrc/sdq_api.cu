@@ -243,20 +243,20 @@ int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, i
                                   void* stream) {
     const char* fn = "sdq_quantized_matmul_epilogue";
     int rc;
-    if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, 1, group_size,
-                                bits, "affine", bias, y, y_dtype, fn)))
-        return rc;
     if (act != SDQ_ACT_NONE && act != SDQ_ACT_GELU_TANH && act != SDQ_ACT_SILU)
         return fail(SDQ_ERR_INVALID, "%s: act must be SDQ_ACT_NONE, _GELU_TANH or _SILU; got %d", fn, act);
     if ((gate && !aligned(gate, 2)) || (residual && !aligned(residual, 2)))
         return fail(SDQ_ERR_INVALID, "%s: misaligned gate or residual (bf16 needs 2 bytes)", fn);
-    if (residual && residual != y) {
+    if (residual && residual != y && m > 0 && n > 0) {     // bad shapes: validate_qmm reports them
         // Partial overlap would let one tile read what another already wrote.
         const uintptr_t r0 = reinterpret_cast<uintptr_t>(residual), y0 = reinterpret_cast<uintptr_t>(y);
         const uintptr_t bytes = static_cast<uintptr_t>(m) * static_cast<uintptr_t>(n) * 2;
         if (r0 < y0 + bytes && y0 < r0 + bytes)
             return fail(SDQ_ERR_INVALID, "%s: residual overlaps y without being y", fn);
     }
+    if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, 1, group_size,
+                                bits, "affine", bias, y, y_dtype, fn)))
+        return rc;
     EpiArgs epi = bias_only(bias);
     epi.act = act;
     epi.gate = static_cast<const uint16_t*>(gate);

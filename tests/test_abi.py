@@ -117,3 +117,48 @@ def test_sharded_argument_checks():
     buf = (ctypes.c_uint8 * 128)()
     assert L.sdq_comm_init(buf, 2, 5, ctypes.byref(h)) == _abi.SDQ_ERR_INVALID
     assert "rank" in _abi.last_error()
+
+
+# ---------------------------------------------------------------- later entry points
+
+def test_gguf_bytes_follow_the_block_table():
+    L = _abi.lib()
+    table = {0: (1, 4), 1: (1, 2), 30: (1, 2), 2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176),
+             14: (256, 210)}
+    for kind, (per, nb) in table.items():
+        assert L.sdq_gguf_bytes(kind, 4 * 256) == 4 * 256 // per * nb
+    assert L.sdq_gguf_bytes(12, 100) == 0          # not whole blocks
+    assert L.sdq_gguf_bytes(3, 256) == 0           # Q4_1: not supported
+
+
+@pytest.mark.parametrize("kind,n,k,bits,code,needle", [
+    (3, 4, 256, 4, _abi.SDQ_ERR_UNSUPPORTED, "GGML type 3"),
+    (12, 4, 320, 4, _abi.SDQ_ERR_INVALID, "whole blocks"),
+    (12, 4, 100, 4, _abi.SDQ_ERR_INVALID, "multiple of the group size"),
+    (12, 4, 256, 3, _abi.SDQ_ERR_UNSUPPORTED, "bits 3"),
+])
+def test_gguf_quantize_rejects_bad_arguments(kind, n, k, bits, code, needle):
+    L = _abi.lib()
+    p = ctypes.c_void_p(0x10000)
+    rc = L.sdq_gguf_quantize(p, kind, n, k, 64, bits, p, p, p, _abi.SDQ_BF16, None)
+    assert rc == code and needle in _abi.last_error()
+    rc = L.sdq_gguf_dequantize(p, 3, 256, p, _abi.SDQ_F32, None)
+    assert rc == _abi.SDQ_ERR_UNSUPPORTED
+
+
+def test_epilogue_rejects_an_unknown_activation_and_a_partial_overlap():
+    L = _abi.lib()
+    p = ctypes.c_void_p(0x10000)
+    rc = L.sdq_quantized_matmul_epilogue(p, 1, 4, 128, p, p, p, 1, 64, 64, 4, None, 9, None, None, p, 1, None)
+    assert rc == _abi.SDQ_ERR_INVALID and "act must be" in _abi.last_error()
+    rc = L.sdq_quantized_matmul_epilogue(p, 1, 4, 128, p, p, p, 1, 64, 64, 4, None, 0, None,
+                                         ctypes.c_void_p(0x10000 + 128), p, 1, None)
+    assert rc == _abi.SDQ_ERR_INVALID and "overlaps" in _abi.last_error()
+
+
+def test_comm_output_and_seeded_normals_check_their_arguments():
+    L = _abi.lib()
+    out = ctypes.c_void_p()
+    assert L.sdq_comm_output(None, 4, 4, ctypes.byref(out)) == _abi.SDQ_ERR_INVALID
+    assert L.sdq_seeded_normals(1, -1, None, None) == _abi.SDQ_ERR_INVALID
+    assert L.sdq_seeded_normals(1, 0, None, None) == _abi.SDQ_OK
