@@ -17,11 +17,15 @@ A step is one quantised matmul over the workload's X with the weight resident in
 With N > 1 ranks each rank holds one workload-sized column shard of a weight N times
 as wide (weak scaling) and the [M, N*n] output is all-gathered over NVLink (NCCL).
 
-Timing: W untimed warm-up steps, then K timed steps bracketed by barrier + synchronize;
-L2 is flushed (a 256 MiB write) before every step outside the timed events, and each
-step is timed with CUDA events on the launching stream; the total is max-reduced over
-ranks.  `e2e` repeats the step through the public API with the step's X copied from
-pinned host memory and the (gathered) Y copied back inside the timed region.
+Timing: W untimed warm-up steps, then K timed steps bracketed by barrier + synchronize.
+For cfg1/2/3/5 the K steps run back to back over R rotating copies of the inputs (X, packed
+W, scales, biases, Y) that together exceed twice the L2, so no step finds its inputs in L2;
+one pair of CUDA events on the launching stream brackets them, and on one GPU the K
+launches are replayed as one CUDA graph.  cfg4 and encoders time each step with its own
+events after a 256 MiB L2-flushing write.  The total is max-reduced over ranks.  `e2e`
+repeats the step eagerly through the public API with the step's X copied from pinned host
+memory and the (gathered) Y copied back inside the timed region (L2 flushed before each
+step, outside its events).
 """
 from __future__ import annotations
 
