@@ -188,6 +188,23 @@ def test_identity_activation_reproduces_the_dequantised_weight(bits, k, n):
     assert torch.equal(y.view(torch.int16), d.t().contiguous().view(torch.int16))
 
 
+@pytest.mark.parametrize("bits,k,n", [(4, 3072, 1000), (8, 3072, 1000), (4, 4096, 384), (8, 1024, 200)])
+def test_identity_rows_at_sixteen_tokens(bits, k, n):
+    """M = 16 runs the tensor-core kernel with X resident (K = 1024, 3072 and 4096; W4 and W8;
+    N not a multiple of the 128-feature tile).  Sixteen rows of the identity pick sixteen
+    columns of dequant(W)^T, each output one exact product; the windows cover every k, so the
+    A operand of every step is checked against the dequantise kernel bit for bit."""
+    w = torch.randn(n, k, device="cuda", generator=torch.Generator("cuda").manual_seed(k + bits)) * 0.02
+    wq, s, b = sdq.quantize(w, 64, bits)
+    d = sdq.dequantize(wq, s, b, 64, bits)
+    eye = torch.eye(k, device="cuda", dtype=torch.bfloat16)
+    for j0 in range(0, k, 16):
+        y = sdq.quantized_matmul(eye[j0:j0 + 16], wq, s, b, 64, bits)
+        if not torch.equal(y.view(torch.int16), d[:, j0:j0 + 16].t().contiguous().view(torch.int16)):
+            raise AssertionError(f"k window {j0}..{j0 + 15} differs from the dequantised weight")
+    sdq.device_status()
+
+
 @pytest.mark.parametrize("cfg", ["c1", "c2", "c3", "c5"])
 def test_baseline_configs_sampled(cfg):
     """The benchmark configurations at full size; the oracle checks a sample of rows and columns."""
