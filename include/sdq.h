@@ -264,7 +264,10 @@ int sdq_comm_output(void* comm, int64_t m, int64_t n, void** out);
  * SDQ_ERR_INVALID naming the limit).  y must be non-NULL.  The call itself
  * allocates nothing; NCCL's buffers belong to the communicator.  The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  All calls share the array: each
+ * that first call before any stream capture.  The address is cached per device
+ * together with the context's id and looked up again after a cudaDeviceReset.
+ * The call must be made with the communicator's device current (otherwise
+ * SDQ_ERR_INVALID): each GPU has its own copy of the array.  All calls share the array: each
  * call writes every element it reads, so nothing needs clearing, but calls whose
  * work overlaps on the GPU (other streams, other host threads) race on it.
  * No counterpart in the reference: its matmul allocates through MLX.

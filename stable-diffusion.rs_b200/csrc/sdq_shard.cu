@@ -536,22 +536,46 @@ static __device__ __align__(256) uint16_t g_static_shards[kStaticShardElems];
 
 // The array's device address on each device, fetched once with that device current.
 // In host code the name g_static_shards is only a host-side stand-in; kernels and
-// NCCL must be given this address.
+// NCCL must be given this address.  The address belongs to the device's context: a
+// cudaDeviceReset replaces the context (and reloads the module), so the cache also
+// keeps the context's unique id and fetches the address again when it changes.
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_ptr[kMaxDevices] = {};
+unsigned long long g_static_ctx[kMaxDevices] = {};
+
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// The unique id of the calling thread's current context (0 when the driver cannot say).
+unsigned long long current_context_id() {
+    static CtxGetIdFn get_id = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<CtxGetIdFn>(p);
+        return static_cast<CtxGetIdFn>(nullptr);
+    }();
+    unsigned long long id = 0;
+    if (get_id == nullptr || get_id(nullptr, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 cudaError_t static_shards_on_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    // Id 0: no context is current yet (or the driver cannot tell); the lookup below makes
+    // the primary context current, and without an id the address is looked up every call.
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (!g_static_ptr[dev]) {
+    if (!g_static_ptr[dev] || ctx == 0 || g_static_ctx[dev] != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_static_shards);
         if (e != cudaSuccess) return e;
         g_static_ptr[dev] = p;
+        g_static_ctx[dev] = current_context_id();
     }
     *out = g_static_ptr[dev];
     return cudaSuccess;
@@ -587,8 +611,18 @@ int sdq_quantized_matmul_sharded_static(const void* x, sdq_dtype x_dtype, int64_
                       fn, need, kStaticShardElems, kStaticShardBytes >> 20);
         return sdq::set_error_message(SDQ_ERR_INVALID, t_static_msg);
     }
+    // Every GPU holds its own copy of the array: a call made with another device current
+    // would hand NCCL (bound to the communicator's device) another GPU's copy.
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess && dev != c->device) {
+        std::snprintf(t_static_msg, sizeof t_static_msg,
+                      "%s: the current device is %d but the communicator belongs to device %d", fn, dev,
+                      c->device);
+        return sdq::set_error_message(SDQ_ERR_INVALID, t_static_msg);
+    }
     void* scratch = nullptr;
-    const cudaError_t e = static_shards_on_current_device(&scratch);
+    if (e == cudaSuccess) e = static_shards_on_current_device(&scratch);
     if (e != cudaSuccess) {
         std::snprintf(t_static_msg, sizeof t_static_msg,
                       "%s: cudaGetSymbolAddress of the static scratch: %s", fn, cudaGetErrorString(e));

@@ -205,6 +205,21 @@ def test_identity_rows_at_sixteen_tokens(bits, k, n):
     sdq.device_status()
 
 
+@pytest.mark.parametrize("m", [1, 2, 4, 8])
+def test_config3_full_size_every_m(m):
+    """Benchmark configuration 3 at full size and at every M it names: X [M, 3072] against the
+    whole [18432, 3072] W4 weight (the adaLN modulation shape), every output checked against the
+    oracle's f64 product of the dequantised weights, on the SeededRng draw of the benchmark."""
+    k, n, bits = 3072, 18432, 4
+    xb, w = O.synthetic_linear(300 + m, m, k, n, 0.02)
+    rwq, rs, rb = O.quantize(w, bits)
+    y = sdq.quantized_matmul(dev_bf16(xb), dev_u32(rwq), dev_bf16(rs), dev_bf16(rb), 64, bits)
+    sdq.device_status()
+    assert y.shape == (m, n)
+    want = O.qmatmul(xb, rwq, rs, rb, n, bits)
+    assert_close(y, want, f"config 3 m={m}")
+
+
 @pytest.mark.parametrize("cfg", ["c1", "c2", "c3", "c5"])
 def test_baseline_configs_sampled(cfg):
     """The benchmark configurations at full size; the oracle checks a sample of rows and columns."""

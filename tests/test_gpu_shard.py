@@ -125,3 +125,67 @@ def test_two_gpu_sharded_linear_reassembles_the_full_product(bits, m, into_comm_
         else:
             # M <= 8 runs the weight-stream kernel, whose k-split follows N: tolerance only
             assert rel <= 1e-2, f"rank {rank}: max-abs-rel {rel:.3e}"
+
+
+def _static_rank_main(rank, world, port, m, k, n, bits, q):
+    """Both ranks call the no-allocation entry point twice; each result must equal what the
+    caller-buffer entry point gives for the same shard, bit for bit."""
+    import ctypes
+    import datetime
+    import torch.distributed as dist
+    from sdq import _abi
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        uid = [sdq.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = sdq.Comm(uid[0], world, rank)
+        try:
+            wq, s, b = _weights(n, k, bits, "cuda")
+            lo, hi = sdq.shard_rows(n, world, rank)
+            wl, sl, bl = wq[lo:hi].contiguous(), s[lo:hi].contiguous(), b[lo:hi].contiguous()
+            same = True
+            for call in range(2):       # the second call finds the first call's contents in the array
+                x = _x(m, k, "cuda", seed=8 + call)
+                want, _ = sdq.quantized_matmul_sharded(x, wl, sl, bl, comm, 64, bits)
+                y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
+                _abi.check(_abi.lib().sdq_quantized_matmul_sharded_static(
+                    ctypes.c_void_p(x.data_ptr()), _abi.SDQ_BF16, m, k, ctypes.c_void_p(wl.data_ptr()),
+                    ctypes.c_void_p(sl.data_ptr()), ctypes.c_void_p(bl.data_ptr()), _abi.SDQ_BF16, hi - lo,
+                    64, bits, None, ctypes.c_void_p(y.data_ptr()), _abi.SDQ_BF16, comm.handle,
+                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+                torch.cuda.synchronize()
+                sdq.device_status()
+                same = same and torch.equal(y.view(torch.int16), want.view(torch.int16))
+            q.put((rank, same, 0.0))
+        finally:
+            comm.destroy()
+            dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m", [4, 300])
+def test_two_gpu_static_scratch_entry_point(bits, m):
+    """The no-allocation sharded entry point on two ranks: NCCL all-gathers the peers' blocks
+    into each rank's static array and the permute reads them back out of it."""
+    import torch.multiprocessing as mp
+    world, k, n = 2, 512, 1024
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_static_rank_main, args=(r, world, port, m, k, n, bits, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same, err in sorted(results):
+        assert same is not None, f"rank {rank}: {err}"
+        assert same, f"rank {rank}: static-scratch result differs from the caller-buffer one"

@@ -58,6 +58,9 @@ def test_static_scratch_matches_the_caller_buffer_entry_point_on_two_calls(bits,
             y = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
             _abi.check(_static(x, wq, s, b, comm, bits, y, bias))
             sdq.device_status()
+            # The same kernel on the same inputs: the results must agree bit for bit; the
+            # tolerance check against the oracle's bar is kept as the looser statement.
+            assert torch.equal(y.view(torch.int16), want.view(torch.int16)), f"call {call}: differs"
             rel, cos = _close(y, want)
             assert rel <= MAX_ABS_REL and cos >= MIN_COSINE, (
                 f"call {call}: max-abs-rel {rel:.3e}, cosine {cos:.7f}")
@@ -79,3 +82,21 @@ def test_static_scratch_rejects_sizes_beyond_its_limit():
         comm.destroy()
     assert rc == _abi.SDQ_ERR_INVALID
     assert "static scratch" in msg
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_static_scratch_rejects_a_call_on_another_device():
+    """Each GPU holds its own copy of the array; a call made with a device current other than
+    the communicator's is refused before anything runs."""
+    comm = sdq.Comm(sdq.Comm.unique_id(), 1, 0)           # bound to device 0
+    try:
+        with torch.cuda.device(1):
+            x = torch.zeros(4, 64, device="cuda", dtype=torch.bfloat16)
+            wq, s, b = sdq.quantize(torch.zeros(64, 64, device="cuda"), 64, 4)
+            y = torch.empty(4, 64, device="cuda", dtype=torch.bfloat16)
+            rc = _static(x, wq, s, b, comm, 4, y)
+            msg = _abi.last_error()
+    finally:
+        comm.destroy()
+    assert rc == _abi.SDQ_ERR_INVALID
+    assert "communicator belongs to device" in msg
