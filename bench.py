@@ -14,6 +14,10 @@ Workloads (the benchmark plan's configurations; data synthetic, seeded):
         a step replays the forward's linears as one CUDA graph (value), and the whole forward
         (attention and elementwise work included) is timed beside it
 A step is one quantised matmul over the workload's X with the weight resident in HBM.
+The default line (cfg2) also carries `secondary`: configs 1, 3 (M = 1, 2, 4, 8) and 5 on
+one GPU, each measured the same way with its own device time, roofline fraction and clocks;
+and `strong_scaling`: config 5's fixed layer split over the N ranks along its output
+features, timed as the GEMM alone and as GEMM + exchange (max over ranks).
 With N > 1 ranks each rank holds one workload-sized column shard of a weight N times
 as wide (weak scaling) and the [M, N*n] output is all-gathered over NVLink (NCCL).
 
@@ -458,6 +462,140 @@ def run_encoders(args, rank, world, local):
         }))
 
 
+def _draw(wl_seed, m, k, n_total, sig, rank_rows, dev):
+    """The benchmark's inputs: the reference's SeededRng draw (X first, then the whole W), X
+    rounded to bf16 and the W rows [lo, hi) quantised by the library."""
+    import torch
+    import sdq
+    lo, hi = rank_rows
+    vals = sdq.seeded_normals(wl_seed, m * k + n_total * k, device=dev)
+    x = (vals[: m * k] * 1.0).view(m, k).to(torch.bfloat16)
+    w = (vals[m * k + lo * k: m * k + hi * k] * sig).view(hi - lo, k)
+    return x, w.contiguous()
+
+
+def measure_single(name, m, k, n, bits, sig, seed, steps, warmup, dev, local):
+    """One workload on one GPU, as the headline is measured: K launches back to back over
+    rotating input copies larger than twice L2, replayed as one CUDA graph between one pair
+    of events, with clocks sampled meanwhile.  Returns the per-workload record of the
+    `secondary` block."""
+    import torch
+    import sdq
+    kind = "tflops" if m > 8 else "gbs"
+    x, w = _draw(seed, m, k, n, sig, (0, n), dev)
+    wq, s, b = sdq.quantize(w, 64, bits)
+    del w
+    set_bytes = m * k * 2 + wq.numel() * 4 + (s.numel() + b.numel()) * 2 + m * n * 2
+    rot = int(min(16, max(2, -(-2 * L2_BYTES // set_bytes))))
+    sets = [(x, wq, s, b)] + [(x.clone(), wq.clone(), s.clone(), b.clone()) for _ in range(rot - 1)]
+    ys = [torch.empty((m, n), device=dev, dtype=torch.bfloat16) for _ in range(rot)]
+
+    def step(i):
+        xi, wqi, si, bi = sets[i % rot]
+        sdq.quantized_matmul(xi, wqi, si, bi, 64, bits, out=ys[i % rot])
+
+    for i in range(max(warmup, rot)):
+        step(i)
+    sdq.device_status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            step(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    sdq.device_status()
+    ms = ev0.elapsed_time(ev1) / steps
+    flops, byts = algorithmic(m, k, n, bits)
+    hbm, tc, src = peaks()
+    if kind == "tflops":
+        value, unit, peak = flops / (ms * 1e-3) / 1e12, "TFLOP/s", tc
+    else:
+        value, unit, peak = byts / (ms * 1e-3) / 1e9, "GB/s", hbm
+    del graph, sets, ys
+    torch.cuda.empty_cache()
+    return {"workload": name, "M": m, "K": k, "N": n, "bits": bits, "value": value, "unit": unit,
+            "kernel_ms": ms, "bound": "tensor" if kind == "tflops" else "hbm", "peak": peak,
+            "frac": value / peak, "peak_source": f"{src} ({'burst bf16' if kind == 'tflops' else 'copy bandwidth'}, MEASURED_PEAKS.json)",
+            "rotating_input_sets": rot, "clocks": clk.summary()}
+
+
+def secondary_workloads(args, dev, local):
+    """The rest of the benchmark plan's metric beside the headline: config 1 (W4, TFLOP/s),
+    config 3 at every M it names (W4, HBM GB/s), config 5 on one GPU (W4, TFLOP/s)."""
+    out = []
+    for name, (m, k, n, bits, sig, _) in (("cfg1", WORKLOADS["cfg1"]), ("cfg5", WORKLOADS["cfg5"])):
+        out.append(measure_single(name, m, k, n, bits, sig, SEEDS[name], args.steps, args.warmup, dev, local))
+    m3, k3, n3, b3, s3, _ = WORKLOADS["cfg3"]
+    for m in (1, 2, 4, 8):
+        out.append(measure_single(f"cfg3_m{m}", m, k3, n3, b3, s3, SEEDS["cfg3"], args.steps, args.warmup, dev, local))
+    return out
+
+
+def strong_scaling_cfg5(args, rank, world, dev, comm, dist):
+    """Config 5 as specified: one fixed layer (X [16384, 3072], W [12288, 3072] W4) split over
+    the ranks along N.  Returns the GEMM-only time (each rank's shard, no exchange) and the
+    GEMM + exchange time (the sharded call, its output assembled on every rank), max over
+    ranks, with the aggregate TFLOP/s of the whole layer."""
+    import torch
+    import sdq
+    m, k, n_total, bits, sig, _ = WORKLOADS["cfg5"]
+    if n_total % world:
+        return None
+    nl = n_total // world
+    x, w = _draw(SEEDS["cfg5"], m, k, n_total, sig, (rank * nl, (rank + 1) * nl), dev)
+    wq, s, b = sdq.quantize(w, 64, bits)
+    del w
+    y_local = torch.empty((m, nl), device=dev, dtype=torch.bfloat16)
+    y_shards = torch.empty((world, m, nl), device=dev, dtype=torch.bfloat16)
+    y_full = comm.output(m, n_total) if comm is not None else torch.empty((m, n_total), device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / steps
+        if dist is not None:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    gemm_ms = timed(lambda: sdq.quantized_matmul(x, wq, s, b, 64, bits, out=y_local), args.steps)
+    if comm is not None:
+        total_ms = timed(lambda: sdq.quantized_matmul_sharded(x, wq, s, b, comm, 64, bits, y_shards=y_shards,
+                                                              out=y_full), args.steps)
+    else:
+        total_ms = gemm_ms
+    sdq.device_status()
+    flops = 2.0 * m * n_total * k
+    hbm, tc, src = peaks()
+    del x, wq, s, b, y_local, y_shards
+    torch.cuda.empty_cache()
+    return {"workload": "cfg5 strong scaling", "M": m, "K": k, "N_total": n_total, "N_per_rank": nl, "bits": bits,
+            "ranks": world, "gemm_ms": gemm_ms, "gemm_tflops": flops / (gemm_ms * 1e-3) / 1e12,
+            "gemm_plus_exchange_ms": total_ms, "gemm_plus_exchange_tflops": flops / (total_ms * 1e-3) / 1e12,
+            "exchange_bytes_received_per_rank": (world - 1) * m * nl * 2,
+            "frac_of_world_peak_gemm": flops / (gemm_ms * 1e-3) / 1e12 / (tc * world),
+            "peak_source": f"{src} burst bf16 x ranks",
+            "timing": "eager calls back to back, events on the launching stream, max over ranks"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,6 +604,8 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=sorted(list(WORKLOADS) + ["cfg4", "encoders"]))
     ap.add_argument("--impl", default="sdq", choices=["sdq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the secondary workloads (configs 1, 3, 5) of the default line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -654,6 +794,18 @@ def main():
     roof["traffic"] = traffic_from_profiles(wl)
     roof["kernel_ms"] = kern_avg
 
+    # The rest of the metric: configs 1, 3 (M = 1, 2, 4, 8) and 5 on one GPU beside the
+    # headline; config 5's strong-scaling split on every run (one GPU: the GEMM alone).
+    secondary = None
+    if world == 1 and wl == "cfg2" and not args.no_secondary:
+        graph = None        # the timed graph is not replayed again: its rotating copies can go
+        del sets, ys
+        torch.cuda.empty_cache()
+        secondary = secondary_workloads(args, dev, local)
+    strong = None
+    if wl == "cfg2" and not args.no_secondary:
+        strong = strong_scaling_cfg5(args, rank, world, dev, comm, dist)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cv, threads, sample = cpu_reference(argparse.Namespace(steps=3, warmup=3), wl)
@@ -691,6 +843,10 @@ def main():
             "gpu_launches": args.steps * (1 if world == 1 or m > 8 else 2),
             "clocks": clk.summary(),
         }
+        if secondary is not None:
+            line["secondary"] = secondary
+        if strong is not None:
+            line["strong_scaling"] = strong
         print(json.dumps(line))
 
 

@@ -147,7 +147,7 @@ int run_qmm(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void*
             const char* fn) {
     const char* msg = nullptr;
     bool taken = false;
-    cudaError_t e = launch_qmv(x, m, k, wq, scales, biases, n, bits, epi, y,
+    cudaError_t e = launch_qmv(x, false, m, k, wq, scales, biases, false, n, bits, epi, y, false,
                                static_cast<cudaStream_t>(stream), &msg, &taken);
     if (e == cudaSuccess && !taken)
         e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, epi, y,

@@ -28,6 +28,8 @@ struct EpiArgs {
     const uint16_t* gate = nullptr;
     const uint16_t* resid = nullptr;
     int act = SDQ_ACT_NONE;
+    // bias, gate and resid hold f32 values instead of bf16 (an f32 output; small-M kernel).
+    bool f32 = false;
     // Whether anything beyond the bias is asked for.
     bool fused() const { return gate != nullptr || resid != nullptr || act != SDQ_ACT_NONE; }
 };
@@ -66,12 +68,14 @@ cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint
                                  const char** msg, uint32_t* done, int chunk_tts, int nchunks,
                                  int grid_cap);
 
-// Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs).
-// Sets *taken = false, launching nothing, for shapes it does not serve (M > 8, or X too
-// large to stay resident beside the weight ring); the caller then uses launch_qmm_tc.
-cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                       const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y,
-                       cudaStream_t st, const char** msg, bool* taken);
+// Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs,
+// programmatic dependent launch).  Sets *taken = false, launching nothing, for what it does
+// not serve (M > 8, X too large to stay resident beside the weight ring, misaligned scales,
+// f32 activations / scales / output); the caller then uses launch_qmm_tc.
+cudaError_t launch_qmv(const void* x, bool x_f32, int64_t m, int64_t k, const uint32_t* wq,
+                       const void* scales, const void* biases, bool sb_f32, int64_t n, int bits,
+                       const EpiArgs& epi, void* y, bool y_f32, cudaStream_t st, const char** msg,
+                       bool* taken);
 
 // GGUF block types (sdq_gguf.cu): values and bytes per block (0 for an unknown type), and
 // the fused dequantise-quantise / the dense dequantise kernels.

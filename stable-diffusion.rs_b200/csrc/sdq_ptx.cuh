@@ -162,6 +162,20 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
     return true;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic-stream-serialisation attribute may start while
+// the previous kernel in its stream is still running.  griddep_wait() returns once that
+// kernel has completed and its memory operations are visible; nothing the earlier kernels
+// write may be read (or overwritten) before it.  griddep_launch_dependents() lets the next
+// kernel of the stream launch early (it still waits in its own griddep_wait()).  Without
+// the attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -172,6 +172,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmW);
     }
     __syncthreads();
+    // Programmatic dependent launch: the next kernel of the stream may launch now (it waits
+    // in its own griddep_wait()); nothing an earlier kernel writes is read before ours.
+    griddep_launch_dependents();
+    griddep_wait();
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
@@ -426,10 +430,21 @@ cudaError_t launch_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, co
     }
     const int64_t tiles = (n + TR - 1) / TR;
     const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    qmv_kernel<BITS, TR><<<grid, kThreads, smem, st>>>(
-        tmW, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
-        epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
-    return cudaGetLastError();
+    // Launched with programmatic stream serialisation, so that back-to-back layers overlap
+    // this kernel's set-up with the previous kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, TR>, tmW, static_cast<const uint16_t*>(x),
+                              static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases), epi,
+                              static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
 }
 
 template <int BITS, int TR>
@@ -485,11 +500,13 @@ cudaError_t launch_bits(const void* x, int64_t m, int64_t k, const uint32_t* wq,
 
 }  // namespace
 
-cudaError_t launch_qmv(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
-                       const void* biases, int64_t n, int bits, const EpiArgs& epi, void* y,
-                       cudaStream_t st, const char** msg, bool* taken) {
+cudaError_t launch_qmv(const void* x, bool x_f32, int64_t m, int64_t k, const uint32_t* wq,
+                       const void* scales, const void* biases, bool sb_f32, int64_t n, int bits,
+                       const EpiArgs& epi, void* y, bool y_f32, cudaStream_t st, const char** msg,
+                       bool* taken) {
     *taken = false;
-    if (m < 1 || m > 8) return cudaSuccess;
+    // bf16 activations, scales, biases and output only; other dtypes take the tensor-core path.
+    if (m < 1 || m > 8 || x_f32 || sb_f32 || y_f32 || epi.f32) return cudaSuccess;
     return bits == 4 ? launch_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken)
                      : launch_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken);
 }
