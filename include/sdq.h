@@ -30,8 +30,12 @@
  *   Y   [m, n]                   Y = X . dequant(W)^T (+ bias[n])
  *
  * Supported today: group_size 64, bits 4 or 8, mode "affine", transpose true,
- * k % 64 == 0, X/Y/S/B bf16 (weights to quantise: f32 or bf16).  Anything
- * else is rejected with SDQ_ERR_UNSUPPORTED or SDQ_ERR_INVALID and a message.
+ * k % 64 == 0; W, S, B, X and Y bf16 or f32 in sdq_quantize, sdq_dequantize
+ * and sdq_quantized_matmul (the reference's own tensors are f32), bf16 in the
+ * fused-epilogue and sharded entry points.  Scales and biases hold bf16 values
+ * either way (the quantiser rounds them to bf16 and widens them exactly when
+ * stored as f32); f32 scales passed in are rounded to bf16.  Anything else is
+ * rejected with SDQ_ERR_UNSUPPORTED or SDQ_ERR_INVALID and a message.
  */
 #ifndef SDQ_H
 #define SDQ_H
@@ -93,7 +97,11 @@ int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases,
  * non-NULL), dequantising inside the kernel.  Replaces mlx_quantized_matmul
  * (mlx.rs:386-397) as called by QuantizedArray::matmul (mlx.rs:1952-1975) and,
  * with `bias`, the separate `y.add(bias)` of quantized::linear
- * (crates/sd-models/src/mlx/quantized.rs:314-317).  `transpose` must be true
+ * (crates/sd-models/src/mlx/quantized.rs:314-317).  x, scales/biases and y
+ * are each bf16 or f32 (bias has y's dtype).  f32 x or scales are rounded to
+ * bf16 by a conversion pass on `stream` (stream-ordered scratch from the
+ * device's default memory pool) before the product; an f32 y is the f32
+ * accumulator plus bias, not rounded to bf16.  `transpose` must be true
  * (the reference always passes true).  m >= 1.  For m <= 8 a weight-stream
  * kernel (TMA ring of packed words, mma.sync on the raw codes, HBM-bound)
  * runs when k * bits / 8 is a multiple of 128; every other shape runs the
@@ -205,6 +213,19 @@ int sdq_seeded_normals(uint64_t seed, int64_t count, float* out, void* stream);
  * reference (MLX kernels have no device-side waits).
  */
 int sdq_device_status(void* stream);
+
+/*
+ * Testing hook for the bounded waits; not for production use.  wait_limit_ns
+ * replaces the 2 s limit of every device-side wait of the matmul kernels (0
+ * restores it; otherwise 1 ms .. 2 s).  With withhold_first_copy non-zero the
+ * weight producer of every CTA of the tensor-core and small-M kernels skips its
+ * first copy and the arrival that goes with it, so the consumers' wait on that
+ * stage runs out: the kernel then records its status bit, lets the copies it
+ * did start land, frees its tensor memory and returns, and sdq_device_status
+ * reports SDQ_ERR_TIMEOUT.  Settings hold for the current device until changed.
+ * Synchronises `stream`.  No counterpart in the reference.
+ */
+int sdq_debug_wait_hook(uint64_t wait_limit_ns, int withhold_first_copy, void* stream);
 
 /*
  * Communicators for the column-sharded linear.  The library owns its NCCL

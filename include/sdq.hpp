@@ -166,7 +166,8 @@ struct QuantizedArray {
     size_t group_size = 64;
     size_t bits = 4;
 
-    // `[out, in]` in, packed `[out, in * bits / 32]` out (mlx.rs:1861-1911).
+    // `[out, in]` in, packed `[out, in * bits / 32]` out (mlx.rs:1861-1911).  The scales and
+    // biases take the weight's dtype, as MLX's do: f32 for the reference's f32 weights.
     static Result<QuantizedArray> quantize(const Array& w, size_t group_size, size_t bits,
                                            const Stream& s) {
         if (w.shape().size() != 2) return Error{SDQ_ERR_INVALID, "sdq: quantize: weight must be 2-D"};
@@ -177,8 +178,9 @@ struct QuantizedArray {
             return error_from(rc, "quantize");
         }
         auto wq = Array::empty({n, k * (int64_t)bits / 32}, kPackedWords);
-        auto sc = Array::empty({n, k / (int64_t)group_size}, SDQ_BF16);
-        auto bi = Array::empty({n, k / (int64_t)group_size}, SDQ_BF16);
+        const sdq_dtype sbt = w.dtype() == SDQ_F32 ? SDQ_F32 : SDQ_BF16;
+        auto sc = Array::empty({n, k / (int64_t)group_size}, sbt);
+        auto bi = Array::empty({n, k / (int64_t)group_size}, sbt);
         if (wq.is_err()) return wq.error();
         if (sc.is_err()) return sc.error();
         if (bi.is_err()) return bi.error();
@@ -186,25 +188,27 @@ struct QuantizedArray {
                          group_size, bits};
         int rc = sdq_quantize(w.data(), w.dtype(), n, k, (int)group_size, (int)bits, "affine",
                               static_cast<uint32_t*>(q.weight.data()), q.scales.data(), q.biases.data(),
-                              SDQ_BF16, s.raw());
+                              sbt, s.raw());
         if (rc != SDQ_OK) return error_from(rc, "quantize");
         return q;
     }
 
-    // Reconstruct the dense array (tests and dense-only layers; mlx.rs:1913-1945).
+    // Reconstruct the dense array in the scales' dtype, as MLX does (tests and dense-only
+    // layers; mlx.rs:1913-1945).
     Result<Array> dequantize(const Stream& s) const {
         const int64_t n = weight.shape()[0], k = weight.shape()[1] * 32 / (int64_t)bits;
-        auto out = Array::empty({n, k}, SDQ_BF16);
+        auto out = Array::empty({n, k}, scales.dtype());
         if (out.is_err()) return out;
         Array o = std::move(out).unwrap();
         int rc = sdq_dequantize(static_cast<const uint32_t*>(weight.data()), scales.data(), biases.data(),
-                                SDQ_BF16, n, k, (int)group_size, (int)bits, "affine", o.data(), SDQ_BF16,
+                                scales.dtype(), n, k, (int)group_size, (int)bits, "affine", o.data(), o.dtype(),
                                 s.raw());
         if (rc != SDQ_OK) return error_from(rc, "dequantize");
         return o;
     }
 
-    // x @ weight.T, dequantising inside the kernel (mlx.rs:1947-1975).  x is [.., in] bf16.
+    // x @ weight.T, dequantising inside the kernel (mlx.rs:1947-1975).  x is [.., in] bf16 or
+    // f32; the result has x's dtype (f32 in, f32 out, as the reference's f32 activations get).
     Result<Array> matmul(const Array& x, const Stream& s, const Array* bias = nullptr) const {
         const int64_t k = x.shape().back();
         int64_t m = 1;
@@ -212,18 +216,19 @@ struct QuantizedArray {
         const int64_t n = weight.shape()[0];
         std::vector<int64_t> oshape(x.shape().begin(), x.shape().end() - 1);
         oshape.push_back(n);
-        auto out = Array::empty(oshape, SDQ_BF16);
+        auto out = Array::empty(oshape, x.dtype());
         if (out.is_err()) return out;
         Array y = std::move(out).unwrap();
         int rc = sdq_quantized_matmul(x.data(), x.dtype(), m, k, static_cast<const uint32_t*>(weight.data()),
-                                      scales.data(), biases.data(), SDQ_BF16, n, 1, (int)group_size,
-                                      (int)bits, "affine", bias ? bias->data() : nullptr, y.data(), SDQ_BF16,
+                                      scales.data(), biases.data(), scales.dtype(), n, 1, (int)group_size,
+                                      (int)bits, "affine", bias ? bias->data() : nullptr, y.data(), y.dtype(),
                                       s.raw());
         if (rc != SDQ_OK) return error_from(rc, "quantized_matmul");
         return y;
     }
 
-    // Packed words plus both scale tensors, counted at 4 bytes each (mlx.rs:1981-1985).
+    // Packed words plus both scale tensors, counted at 4 bytes each whatever they are stored as
+    // (mlx.rs:1981-1985).
     size_t resident_bytes() const {
         return (size_t)weight.elem_count() * 4 + (size_t)(scales.elem_count() + biases.elem_count()) * 4;
     }

@@ -132,10 +132,12 @@ int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const u
                     "%s: transpose=false is not supported (weights are [out, in]; pass true)", fn);
     if (!x || !wq || !scales || !biases || !y)
         return fail(SDQ_ERR_INVALID, "%s: x, wq, scales, biases and y must be non-null", fn);
-    if (x_dtype != SDQ_BF16 || y_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16)
-        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16", fn);
-    if (!aligned(x, 16) || !aligned(wq, 16) || !aligned(y, 2) || !aligned(scales, 2) ||
-        !aligned(biases, 2) || (bias && !aligned(bias, 2)))
+    auto bf_or_f32 = [](sdq_dtype d) { return d == SDQ_BF16 || d == SDQ_F32; };
+    if (!bf_or_f32(x_dtype) || !bf_or_f32(y_dtype) || !bf_or_f32(sb_dtype))
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16 or f32", fn);
+    const size_t ye = y_dtype == SDQ_F32 ? 4 : 2, se = sb_dtype == SDQ_F32 ? 4 : 2;
+    if (!aligned(x, 16) || !aligned(wq, 16) || !aligned(y, ye) || !aligned(scales, se) ||
+        !aligned(biases, se) || (bias && !aligned(bias, ye)))
         return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (x and wq need 16 bytes)", fn);
     return check_device();
 }
@@ -147,7 +149,7 @@ int run_qmm(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void*
             const char* fn) {
     const char* msg = nullptr;
     bool taken = false;
-    cudaError_t e = launch_qmv(x, false, m, k, wq, scales, biases, false, n, bits, epi, y, false,
+    cudaError_t e = launch_qmv(x, false, m, k, wq, scales, biases, false, n, bits, epi, y, epi.f32,
                                static_cast<cudaStream_t>(stream), &msg, &taken);
     if (e == cudaSuccess && !taken)
         e = launch_qmm_tc(x, m, k, wq, scales, biases, n, bits, epi, y,
@@ -187,16 +189,17 @@ int sdq_quantize(const void* w, sdq_dtype w_dtype, int64_t n, int64_t k, int gro
         return fail(SDQ_ERR_INVALID, "%s: w, wq, scales and biases must be non-null", fn);
     if (w_dtype != SDQ_F32 && w_dtype != SDQ_BF16)
         return fail(SDQ_ERR_UNSUPPORTED, "%s: weights must be f32 or bf16 (dtype %d)", fn, (int)w_dtype);
-    if (sb_dtype != SDQ_BF16)
-        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 only (dtype %d)", fn,
+    if (sb_dtype != SDQ_BF16 && sb_dtype != SDQ_F32)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 or f32 (dtype %d)", fn,
                     (int)sb_dtype);
-    if (!aligned(w, w_dtype == SDQ_F32 ? 8 : 4) || !aligned(wq, 4) || !aligned(scales, 2) ||
-        !aligned(biases, 2))
-        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (w needs %d bytes, wq 4, scales/biases 2)",
-                    fn, w_dtype == SDQ_F32 ? 8 : 4);
+    const size_t se = sb_dtype == SDQ_F32 ? 4 : 2;
+    if (!aligned(w, w_dtype == SDQ_F32 ? 8 : 4) || !aligned(wq, 4) || !aligned(scales, se) ||
+        !aligned(biases, se))
+        return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (w needs %d bytes, wq 4, scales/biases %d)",
+                    fn, w_dtype == SDQ_F32 ? 8 : 4, (int)se);
     if ((rc = check_device())) return rc;
     cudaError_t e = launch_quantize(w, w_dtype == SDQ_BF16, n, k, bits, wq, scales, biases,
-                                    static_cast<cudaStream_t>(stream));
+                                    sb_dtype == SDQ_F32, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("sdq_quantize: kernel launch", e);
     return ok();
 }
@@ -210,15 +213,16 @@ int sdq_dequantize(const uint32_t* wq, const void* scales, const void* biases, s
     if ((rc = check_nk(n, k, fn))) return rc;
     if (!wq || !scales || !biases || !out)
         return fail(SDQ_ERR_INVALID, "%s: wq, scales, biases and out must be non-null", fn);
-    if (sb_dtype != SDQ_BF16)
-        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases are stored bf16 only", fn);
+    if (sb_dtype != SDQ_BF16 && sb_dtype != SDQ_F32)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: scales/biases must be bf16 or f32", fn);
     if (out_dtype != SDQ_BF16 && out_dtype != SDQ_F32)
         return fail(SDQ_ERR_UNSUPPORTED, "%s: output must be bf16 or f32", fn);
-    if (!aligned(wq, 4) || !aligned(out, 16) || !aligned(scales, 2) || !aligned(biases, 2))
+    const size_t se = sb_dtype == SDQ_F32 ? 4 : 2;
+    if (!aligned(wq, 4) || !aligned(out, 16) || !aligned(scales, se) || !aligned(biases, se))
         return fail(SDQ_ERR_INVALID, "%s: misaligned pointer (out needs 16 bytes)", fn);
     if ((rc = check_device())) return rc;
-    cudaError_t e = launch_dequantize(wq, scales, biases, n, k, bits, out, out_dtype == SDQ_F32,
-                                      static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_dequantize(wq, scales, biases, sb_dtype == SDQ_F32, n, k, bits, out,
+                                      out_dtype == SDQ_F32, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("sdq_dequantize: kernel launch", e);
     return ok();
 }
@@ -232,7 +236,41 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
     if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, transpose,
                                 group_size, bits, mode, bias, y, y_dtype, fn)))
         return rc;
-    return run_qmm(x, m, k, wq, scales, biases, n, bits, bias_only(bias), y, stream, fn);
+    EpiArgs epi = bias_only(bias);
+    epi.f32 = y_dtype == SDQ_F32;
+    if (x_dtype == SDQ_BF16 && sb_dtype == SDQ_BF16)
+        return run_qmm(x, m, k, wq, scales, biases, n, bits, epi, y, stream, fn);
+    // f32 activations or scales: the tensor cores take bf16, so they are rounded (nearest
+    // even) into stream-ordered temporaries first -- the one place the library allocates on
+    // the compute path, through the stream's memory pool.  Scales and biases from
+    // sdq_quantize are bf16 values already and stay exact.
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t xb = x_dtype == SDQ_F32 ? ((size_t)m * k * 2 + 255) & ~(size_t)255 : 0;
+    const size_t sbb = sb_dtype == SDQ_F32 ? ((size_t)n * (k / 64) * 2 + 255) & ~(size_t)255 : 0;
+    uint8_t* tmp = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&tmp), xb + 2 * sbb, st);
+    if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: cudaMallocAsync (f32 inputs)", e);
+    const void* xk = x;
+    const void* sk = scales;
+    const void* bk = biases;
+    if (x_dtype == SDQ_F32) {
+        e = launch_f32_to_bf16(static_cast<const float*>(x), tmp, m * k, st);
+        xk = tmp;
+    }
+    if (e == cudaSuccess && sb_dtype == SDQ_F32) {
+        e = launch_f32_to_bf16(static_cast<const float*>(scales), tmp + xb, n * (k / 64), st);
+        if (e == cudaSuccess) e = launch_f32_to_bf16(static_cast<const float*>(biases), tmp + xb + sbb, n * (k / 64), st);
+        sk = tmp + xb;
+        bk = tmp + xb + sbb;
+    }
+    if (e != cudaSuccess) {
+        cudaFreeAsync(tmp, st);
+        return cuda_fail("sdq_quantized_matmul: f32 -> bf16 conversion", e);
+    }
+    rc = run_qmm(xk, m, k, wq, sk, bk, n, bits, epi, y, stream, fn);
+    e = cudaFreeAsync(tmp, st);
+    if (rc == SDQ_OK && e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: cudaFreeAsync", e);
+    return rc;
 }
 
 int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
@@ -257,6 +295,8 @@ int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, i
     if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, 1, group_size,
                                 bits, "affine", bias, y, y_dtype, fn)))
         return rc;
+    if (x_dtype != SDQ_BF16 || y_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16)
+        return fail(SDQ_ERR_UNSUPPORTED, "%s: x, y, scales and biases must be bf16", fn);
     EpiArgs epi = bias_only(bias);
     epi.act = act;
     epi.gate = static_cast<const uint16_t*>(gate);
@@ -330,6 +370,20 @@ int sdq_seeded_normals(uint64_t seed, int64_t count, float* out, void* stream) {
     if ((rc = check_device())) return rc;
     cudaError_t e = launch_seeded_normals(seed, count, out, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("sdq_seeded_normals: kernel launch", e);
+    return ok();
+}
+
+int sdq_debug_wait_hook(uint64_t wait_limit_ns, int withhold_first_copy, void* stream) {
+    if (wait_limit_ns != 0 && (wait_limit_ns < 1000000ull || wait_limit_ns > 2000000000ull))
+        return fail(SDQ_ERR_INVALID, "sdq_debug_wait_hook: wait_limit_ns must be 0 or in [1 ms, 2 s], got %llu",
+                    (unsigned long long)wait_limit_ns);
+    int rc;
+    if ((rc = check_device())) return rc;
+    const unsigned long long lim = wait_limit_ns == 0 ? 2000000000ull : wait_limit_ns;
+    const int wh = withhold_first_copy != 0;
+    cudaError_t e = set_wait_hook_tc(lim, wh, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = set_wait_hook_qmv(lim, wh, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail("sdq_debug_wait_hook", e);
     return ok();
 }
 

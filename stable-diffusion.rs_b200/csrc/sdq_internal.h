@@ -28,7 +28,8 @@ struct EpiArgs {
     const uint16_t* gate = nullptr;
     const uint16_t* resid = nullptr;
     int act = SDQ_ACT_NONE;
-    // bias, gate and resid hold f32 values instead of bf16 (an f32 output; small-M kernel).
+    // The output y is f32 (written from the f32 accumulator, not rounded) and bias holds f32
+    // values; only the plain output stage (bias alone) has this form.
     bool f32 = false;
     // Whether anything beyond the bias is asked for.
     bool fused() const { return gate != nullptr || resid != nullptr || act != SDQ_ACT_NONE; }
@@ -40,10 +41,12 @@ inline EpiArgs bias_only(const void* bias) {
 }
 
 cudaError_t launch_quantize(const void* w, bool w_bf16, int64_t n, int64_t k, int bits,
-                            uint32_t* wq, void* scales, void* biases, cudaStream_t st);
-cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases,
+                            uint32_t* wq, void* scales, void* biases, bool sb_f32, cudaStream_t st);
+cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, bool sb_f32,
                               int64_t n, int64_t k, int bits, void* out, bool out_f32,
                               cudaStream_t st);
+// f32 -> bf16, round to nearest even (in 16-byte aligned when count >= 8, out 16-byte aligned).
+cudaError_t launch_f32_to_bf16(const float* in, void* out, int64_t count, cudaStream_t st);
 
 // Quantised matmul on the tensor cores (TMA + tcgen05 / TMEM), every M.  Returns a CUDA error
 // or cudaSuccess; `msg` receives a description when tensor-map encoding fails.
@@ -91,5 +94,8 @@ cudaError_t launch_seeded_normals(uint64_t seed, int64_t count, float* out, cuda
 // Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st);
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st);
+// Testing hooks of the two matmul files (wait limit, withheld first copy); synchronise `st`.
+cudaError_t set_wait_hook_tc(unsigned long long limit_ns, int withhold, cudaStream_t st);
+cudaError_t set_wait_hook_qmv(unsigned long long limit_ns, int withhold, cudaStream_t st);
 
 }  // namespace sdq

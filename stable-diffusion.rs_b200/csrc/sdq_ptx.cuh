@@ -17,6 +17,14 @@ namespace sdq {
 // Wall-clock limit for one bounded wait (nanoseconds of %globaltimer).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Testing hooks (set through sdq_debug_wait_hook; every file that includes this header has
+// its own copy, and the hook sets each): the limit the waits use (kWaitLimitNs unless a test
+// shortened it), and a switch that makes the weight producer of every CTA skip its first copy
+// together with the arrival that goes with it, so that the consumers' wait on that stage runs
+// out and the abort path (status bit, drain, TMEM release, early return) is taken.
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+static __device__ int g_withhold_first_copy = 0;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -74,18 +82,18 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
     return ok != 0;
 }
 
-// Wait for the phase with `parity` to complete, giving up after kWaitLimitNs or
+// Wait for the phase with `parity` to complete, giving up after the wait limit or
 // as soon as another role of this CTA has raised `*abort`.  Returns false when
 // it gave up (and then sets the abort flag and the global status bit).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           unsigned int* status, unsigned int status_bit) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
+    const unsigned long long t0 = globaltimer(), lim = g_wait_limit_ns;
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0u) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > lim) {
                 *abort = 1;
                 atomicOr(status, status_bit);
                 return false;
@@ -102,13 +110,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
                                                 unsigned int* status, unsigned int status_bit,
                                                 unsigned int sleep_ns) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer();
+    const unsigned long long t0 = globaltimer(), lim = g_wait_limit_ns;
     for (uint32_t it = 1;; ++it) {
         __nanosleep(sleep_ns);
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 15u) == 0u) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > lim) {
                 *abort = 1;
                 atomicOr(status, status_bit);
                 return false;
@@ -137,12 +145,12 @@ __device__ __forceinline__ bool mbar_wait_warp_parked(uint64_t* bar, uint32_t pa
                                                       unsigned int status_bit, uint32_t hint_ns) {
     bool ok = mbar_try_wait_hint(bar, parity, hint_ns);
     if (!ok) {
-        const unsigned long long t0 = globaltimer();
+        const unsigned long long t0 = globaltimer(), lim = g_wait_limit_ns;
         for (uint32_t it = 1;; ++it) {
             if (mbar_try_wait_hint(bar, parity, hint_ns)) { ok = true; break; }
             if ((it & 7u) == 0u) {
                 if (*abort) break;
-                if (globaltimer() - t0 > kWaitLimitNs) {
+                if (globaltimer() - t0 > lim) {
                     *abort = 1;
                     atomicOr(status, status_bit);
                     break;
@@ -155,9 +163,9 @@ __device__ __forceinline__ bool mbar_wait_warp_parked(uint64_t* bar, uint32_t pa
 
 // Bounded wait used only while draining after an abort: ignores the abort flag.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-    const unsigned long long t0 = globaltimer();
+    const unsigned long long t0 = globaltimer(), lim = g_wait_limit_ns;
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitLimitNs) return false;
+        if (globaltimer() - t0 > lim) return false;
     }
     return true;
 }

@@ -113,8 +113,9 @@ size_t smem_bytes(int64_t k) {
 }
 
 // FUSED: the output stage applies gate / residual / activation (EpiArgs::fused); the plain
-// instantiation adds the bias only and carries none of that code.
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED>
+// instantiation adds the bias only and carries none of that code.  YF32 (plain only): the
+// output is f32, written from the accumulator straight to global memory (bias in f32).
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32>
 __global__ void __launch_bounds__(tc_threads(BITS), 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
@@ -225,13 +226,16 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         if (lane == 0) {
             int it = 0, last_it = -1;
             bool ok = true;
+            const bool withhold = g_withhold_first_copy != 0;   // testing hook, normally false
             for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
                 const int ft = tile % nft;
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % SW;
                     if (!mbar_wait_sleep(wempty + s, ((it / SW) & 1) ^ 1, abort_flag, status, 1u, 32)) { ok = false; break; }
-                    mbar_arrive_expect_tx(wfull + s, C::W_STAGE);
-                    tma_load_2d(sW + s * C::W_STAGE, &tmW, wfull + s, kt * C::W_WORDS, ft * C::BF);
+                    if (!(withhold && it == 0)) {
+                        mbar_arrive_expect_tx(wfull + s, C::W_STAGE);
+                        tma_load_2d(sW + s * C::W_STAGE, &tmW, wfull + s, kt * C::W_WORDS, ft * C::BF);
+                    }
                     last_it = it;
                 }
             }
@@ -387,7 +391,9 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
             const int tt = tile / nft, ft = tile - tt * nft;
             const int f = ft * C::BF + fl;
-            const float badd = (epi.bias != nullptr && f < N) ? bf16_bits_to_f32(epi.bias[f]) : 0.f;
+            float badd = 0.f;
+            if (epi.bias != nullptr && f < N)
+                badd = YF32 ? reinterpret_cast<const float*>(epi.bias)[f] : bf16_bits_to_f32(epi.bias[f]);
             const float gmul = (FUSED && epi.gate != nullptr && f < N) ? bf16_bits_to_f32(epi.gate[f]) : 1.f;
             // The staging chunks of this group must have been read by the previous
             // tile's stores before they are overwritten.
@@ -421,7 +427,18 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                         __syncwarp();
                         tmem_ld16(tmem + lane_base + C::D_COL + (uint32_t)(CW * c + 16 * h), v);
                         tc_wait_ld();
-                        if constexpr (!FUSED) {
+                        if constexpr (YF32) {
+                            // f32 output: each thread writes its feature of 16 tokens; a warp's
+                            // 32 features are 128 contiguous bytes of a token's row.
+                            const int t0 = tt * BT + c * CW + 16 * h;
+                            if (f < N) {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (t0 + j < M)
+                                        reinterpret_cast<float*>(y)[(size_t)(t0 + j) * ldy + f] =
+                                            __uint_as_float(v[j]) + badd;
+                            }
+                        } else if constexpr (!FUSED) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 yrow[(16 * h + j) * C::BF] =
@@ -456,7 +473,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                                          tt * BT + c * CW);
                     bulk_commit_group();
                 }
-            } else if (f < N) {
+            } else if (!YF32 && f < N) {
                 for (int c = e; c < NCH; c += kEpiGroups) {
                     const uint16_t* yrow =
                         reinterpret_cast<const uint16_t*>(sY + (size_t)c * CW * C::BF * 2) + fl;
@@ -502,7 +519,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
 constexpr size_t kMaxSmem = kQmvMaxSmem;
 
 
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED>
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
                         cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
@@ -545,7 +562,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     // base are 16-byte aligned; otherwise the tensor map stays unused and the epilogue stores.
     CUtensorMap tmY;
     std::memset(&tmY, 0, sizeof(tmY));
-    const bool y_tma = (ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
+    const bool y_tma = !YF32 && (ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(y) % 16) == 0;
     if (y_tma) {
         cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
         cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
@@ -584,7 +601,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     if (e != cudaSuccess) return e;
     static bool configured[64] = {};
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED>,
+        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -592,7 +609,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
     const int grid = (int)(tiles < cap ? tiles : cap);
-    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED><<<grid, tc_threads(BITS), smem, st>>>(
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
         ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
@@ -635,10 +652,13 @@ cudaError_t launch_tc_f(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                         const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
                         cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
     if (epi.fused())
-        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
-                                                             msg, sig, grid_cap);
-    return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
-                                                          msg, sig, grid_cap);
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, true, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
+                                                                    msg, sig, grid_cap);
+    if (epi.f32)           // f32 output (the bias, if any, f32 too)
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
+                                                                    msg, sig, grid_cap);
+    return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
+                                                                 msg, sig, grid_cap);
 }
 
 template <int BITS>
@@ -696,6 +716,15 @@ cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint
     const TcSignal sig{done, chunk_tts, nchunks};
     return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap)
                      : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
+}
+
+cudaError_t set_wait_hook_tc(unsigned long long limit_ns, int withhold, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyToSymbolAsync(g_wait_limit_ns, &limit_ns, sizeof(limit_ns), 0,
+                                            cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbolAsync(g_withhold_first_copy, &withhold, sizeof(withhold), 0,
+                                    cudaMemcpyHostToDevice, st);
+    return e == cudaSuccess ? cudaStreamSynchronize(st) : e;
 }
 
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st) {

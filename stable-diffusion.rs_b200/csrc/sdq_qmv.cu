@@ -136,7 +136,7 @@ template <int BITS, int TR>
 __global__ void __launch_bounds__(kThreads, 1)
     qmv_kernel(const __grid_constant__ CUtensorMap tmW, const uint16_t* __restrict__ x,
                const uint16_t* __restrict__ scales, const uint16_t* __restrict__ biases,
-               const EpiArgs epi, uint16_t* y, int M, int N, int K) {
+               const EpiArgs epi, void* y, int M, int N, int K) {
     using C = QmvCfg<BITS, TR>;
     constexpr int SW = C::SW;
     extern __shared__ uint8_t smem_raw[];
@@ -189,12 +189,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         int it = 0, last_it = -1;
         bool ok = true;
+        const bool withhold = g_withhold_first_copy != 0;       // testing hook, normally false
         for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             for (int sg = 0; sg < stages_per_tile; ++sg, ++it) {
                 const int s = it % SW;
                 if (!__all_sync(0xffffffffu, mbar_wait_sleep(wempty + s, ((it / SW) & 1) ^ 1,
                                                              abort_flag, status, 1u, 32))) { ok = false; break; }
-                if (lane == 0) {
+                if (lane == 0 && !(withhold && it == 0)) {
                     mbar_arrive_expect_tx(wfull + s, C::STAGE);
                     tma_load_2d(sW + (size_t)s * C::STAGE, &tmW, wfull + s, sg * 32, tile * TR);
                 }
@@ -375,11 +376,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 auto put = [&](float a, int tok, int row) {
                     if (row >= N || tok >= M) return;
                     const int64_t o = (int64_t)tok * N + row;
+                    if (epi.f32) {          // f32 output, f32 bias (plain output stage only)
+                        if (epi.bias != nullptr) a += reinterpret_cast<const float*>(epi.bias)[row];
+                        static_cast<float*>(y)[o] = a;
+                        return;
+                    }
                     a += epi.bias != nullptr ? bf16_bits_to_f32(epi.bias[row]) : 0.f;
                     a = epi_activation(a, epi.act);
                     if (epi.gate != nullptr) a *= bf16_bits_to_f32(epi.gate[row]);
                     if (epi.resid != nullptr) a += bf16_bits_to_f32(epi.resid[o]);
-                    y[o] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
+                    static_cast<uint16_t*>(y)[o] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
                 };
                 put(acc[0], m0i, r0);
                 put(acc[1], m1i, r0);
@@ -444,7 +450,7 @@ cudaError_t launch_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, co
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, qmv_kernel<BITS, TR>, tmW, static_cast<const uint16_t*>(x),
                               static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases), epi,
-                              static_cast<uint16_t*>(y), (int)m, (int)n, (int)k);
+                              y, (int)m, (int)n, (int)k);
 }
 
 template <int BITS, int TR>
@@ -505,10 +511,19 @@ cudaError_t launch_qmv(const void* x, bool x_f32, int64_t m, int64_t k, const ui
                        const EpiArgs& epi, void* y, bool y_f32, cudaStream_t st, const char** msg,
                        bool* taken) {
     *taken = false;
-    // bf16 activations, scales, biases and output only; other dtypes take the tensor-core path.
-    if (m < 1 || m > 8 || x_f32 || sb_f32 || y_f32 || epi.f32) return cudaSuccess;
+    // bf16 activations, scales and biases (the C ABI converts f32 ones first); bf16 or f32 output.
+    if (m < 1 || m > 8 || x_f32 || sb_f32 || y_f32 != epi.f32) return cudaSuccess;
     return bits == 4 ? launch_bits<4>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken)
                      : launch_bits<8>(x, m, k, wq, scales, biases, n, epi, y, st, msg, taken);
+}
+
+cudaError_t set_wait_hook_qmv(unsigned long long limit_ns, int withhold, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyToSymbolAsync(g_wait_limit_ns, &limit_ns, sizeof(limit_ns), 0,
+                                            cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbolAsync(g_withhold_first_copy, &withhold, sizeof(withhold), 0,
+                                    cudaMemcpyHostToDevice, st);
+    return e == cudaSuccess ? cudaStreamSynchronize(st) : e;
 }
 
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st) {

@@ -9,6 +9,14 @@
 //
 // Dequantise (replaces mlx_dequantize behind QuantizedArray::dequantize,
 // mlx.rs:1918-1945): one thread per packed word, vector stores.
+//
+// Scales and biases may be stored bf16 or f32 (the reference's callers hold f32).  The
+// quantiser's values are bf16 either way (the rule rounds them), widened exactly when stored
+// as f32; f32 scales read by the dequantiser and the matmul are rounded to bf16 (nearest
+// even), which leaves the quantiser's own values unchanged.
+//
+// f32 -> bf16 conversion (the matmul's pre-pass for f32 activations or scales): 8 values
+// per thread, round to nearest even, NaN -> 0x7fff.
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -19,11 +27,11 @@
 
 namespace sdq {
 
-template <int BITS, bool IN_BF16>
+template <int BITS, bool IN_BF16, bool SB_F32>
 __global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ w, int64_t n,
                                                        int64_t k, uint32_t* __restrict__ wq,
-                                                       __nv_bfloat16* __restrict__ scales,
-                                                       __nv_bfloat16* __restrict__ biases) {
+                                                       void* __restrict__ scales,
+                                                       void* __restrict__ biases) {
     const int lane = threadIdx.x & 31;
     const int64_t groups_per_row = k / 64;
     const int64_t total = n * groups_per_row;
@@ -45,14 +53,21 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void* __restrict__ 
             v0 = p.x;
             v1 = p.y;
         }
-        quantize_group_warp<BITS>(v0, v1, lane, gi, row, g, k, wq, scales, biases);
+        quantize_group_warp<BITS, SB_F32>(v0, v1, lane, gi, row, g, k, wq, scales, biases);
     }
 }
 
-template <int BITS, bool OUT_F32>
+// Scale / bias element i as bf16 bits.
+template <bool SB_F32>
+__device__ __forceinline__ uint32_t sb_bits(const void* p, int64_t i) {
+    if (SB_F32) return f32_to_bf16_rne(static_cast<const float*>(p)[i]);
+    return static_cast<const uint16_t*>(p)[i];
+}
+
+template <int BITS, bool OUT_F32, bool SB_F32>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ wq,
-                                                         const __nv_bfloat16* __restrict__ scales,
-                                                         const __nv_bfloat16* __restrict__ biases,
+                                                         const void* __restrict__ scales,
+                                                         const void* __restrict__ biases,
                                                          int64_t n, int64_t k, void* __restrict__ out) {
     constexpr int PER = 32 / BITS;  // elements per word
     const int64_t words_per_row = k / PER;
@@ -63,8 +78,8 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restr
         const int64_t row = i / words_per_row;
         const int64_t wi = i - row * words_per_row;
         const int64_t g = row * groups_per_row + (wi * PER) / 64;
-        const uint32_t sbits = reinterpret_cast<const uint16_t*>(scales)[g];
-        const uint32_t bbits = reinterpret_cast<const uint16_t*>(biases)[g];
+        const uint32_t sbits = sb_bits<SB_F32>(scales, g);
+        const uint32_t bbits = sb_bits<SB_F32>(biases, g);
         const uint32_t w = __ldg(wq + i);
         const int64_t e0 = row * k + wi * PER;
         if (BITS == 4) {
@@ -101,34 +116,58 @@ static int grid_for(int64_t work, int threads, int per_sm_blocks) {
 }
 
 cudaError_t launch_quantize(const void* w, bool w_bf16, int64_t n, int64_t k, int bits,
-                            uint32_t* wq, void* scales, void* biases, cudaStream_t st) {
+                            uint32_t* wq, void* scales, void* biases, bool sb_f32, cudaStream_t st) {
     const int64_t groups = n * (k / 64);
     const int grid = grid_for(groups * 32, 256, 8);
-    auto* s = static_cast<__nv_bfloat16*>(scales);
-    auto* b = static_cast<__nv_bfloat16*>(biases);
+    auto go = [&](auto kern) { kern<<<grid, 256, 0, st>>>(w, n, k, wq, scales, biases); };
     if (bits == 4) {
-        if (w_bf16) quantize_kernel<4, true><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
-        else quantize_kernel<4, false><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+        if (w_bf16) sb_f32 ? go(quantize_kernel<4, true, true>) : go(quantize_kernel<4, true, false>);
+        else sb_f32 ? go(quantize_kernel<4, false, true>) : go(quantize_kernel<4, false, false>);
     } else {
-        if (w_bf16) quantize_kernel<8, true><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
-        else quantize_kernel<8, false><<<grid, 256, 0, st>>>(w, n, k, wq, s, b);
+        if (w_bf16) sb_f32 ? go(quantize_kernel<8, true, true>) : go(quantize_kernel<8, true, false>);
+        else sb_f32 ? go(quantize_kernel<8, false, true>) : go(quantize_kernel<8, false, false>);
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, int64_t n,
-                              int64_t k, int bits, void* out, bool out_f32, cudaStream_t st) {
+cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, bool sb_f32,
+                              int64_t n, int64_t k, int bits, void* out, bool out_f32, cudaStream_t st) {
     const int64_t words = n * k * bits / 32;
     const int grid = grid_for(words, 256, 8);
-    auto* s = static_cast<const __nv_bfloat16*>(scales);
-    auto* b = static_cast<const __nv_bfloat16*>(biases);
+    auto go = [&](auto kern) { kern<<<grid, 256, 0, st>>>(wq, scales, biases, n, k, out); };
     if (bits == 4) {
-        if (out_f32) dequantize_kernel<4, true><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
-        else dequantize_kernel<4, false><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+        if (out_f32) sb_f32 ? go(dequantize_kernel<4, true, true>) : go(dequantize_kernel<4, true, false>);
+        else sb_f32 ? go(dequantize_kernel<4, false, true>) : go(dequantize_kernel<4, false, false>);
     } else {
-        if (out_f32) dequantize_kernel<8, true><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
-        else dequantize_kernel<8, false><<<grid, 256, 0, st>>>(wq, s, b, n, k, out);
+        if (out_f32) sb_f32 ? go(dequantize_kernel<8, true, true>) : go(dequantize_kernel<8, true, false>);
+        else sb_f32 ? go(dequantize_kernel<8, false, true>) : go(dequantize_kernel<8, false, false>);
     }
+    return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ in,
+                                                          uint16_t* __restrict__ out, int64_t count) {
+    const int64_t n8 = count / 8;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = reinterpret_cast<const float4*>(in)[2 * i];
+        const float4 b = reinterpret_cast<const float4*>(in)[2 * i + 1];
+        uint4 o;
+        o.x = f32_to_bf16_rne(a.x) | (f32_to_bf16_rne(a.y) << 16);
+        o.y = f32_to_bf16_rne(a.z) | (f32_to_bf16_rne(a.w) << 16);
+        o.z = f32_to_bf16_rne(b.x) | (f32_to_bf16_rne(b.y) << 16);
+        o.w = f32_to_bf16_rne(b.z) | (f32_to_bf16_rne(b.w) << 16);
+        reinterpret_cast<uint4*>(out)[i] = o;
+    }
+    // The tail of a count that is not a multiple of 8, one value per thread.
+    for (int64_t i = n8 * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = (uint16_t)f32_to_bf16_rne(in[i]);
+}
+
+cudaError_t launch_f32_to_bf16(const float* in, void* out, int64_t count, cudaStream_t st) {
+    const int grid = grid_for(count / 8 + 1, 256, 8);
+    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(in, static_cast<uint16_t*>(out), count);
     return cudaGetLastError();
 }
 

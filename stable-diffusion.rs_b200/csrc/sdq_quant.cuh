@@ -47,13 +47,14 @@ __device__ __forceinline__ uint32_t quant_one(float v, float s, float b, uint32_
 
 // Quantise and pack group gi (row `row`, group g of the row, K values per row) from the
 // warp's values: extrema by a warp-shuffle reduction under a total order, scale and bias
-// rounded to bf16, codes packed little-end into the row's words.
-template <int BITS>
+// rounded to bf16, codes packed little-end into the row's words.  SB_F32 stores the scale
+// and bias as f32 (the same rounded values, widened exactly) for callers that hold f32.
+template <int BITS, bool SB_F32 = false>
 __device__ __forceinline__ void quantize_group_warp(float v0, float v1, int lane, int64_t gi,
                                                     int64_t row, int64_t g, int64_t k,
                                                     uint32_t* __restrict__ wq,
-                                                    __nv_bfloat16* __restrict__ scales,
-                                                    __nv_bfloat16* __restrict__ biases) {
+                                                    void* __restrict__ scales,
+                                                    void* __restrict__ biases) {
     constexpr uint32_t qmax = (1u << BITS) - 1u;
     float mn = tmin(v0, v1), mx = tmax(v0, v1);
     // An all-NaN pair leaves NaN here; the oracle starts from +inf / -inf,
@@ -85,8 +86,13 @@ __device__ __forceinline__ void quantize_group_warp(float v0, float v1, int lane
         if ((lane & 1) == 0) wq[wbase + (lane >> 1)] = v;
     }
     if (lane == 0) {
-        reinterpret_cast<uint16_t*>(scales)[gi] = (uint16_t)sb;
-        reinterpret_cast<uint16_t*>(biases)[gi] = (uint16_t)bb;
+        if (SB_F32) {
+            static_cast<float*>(scales)[gi] = s;
+            static_cast<float*>(biases)[gi] = b;
+        } else {
+            static_cast<uint16_t*>(scales)[gi] = (uint16_t)sb;
+            static_cast<uint16_t*>(biases)[gi] = (uint16_t)bb;
+        }
     }
 }
 

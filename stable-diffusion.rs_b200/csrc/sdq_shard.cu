@@ -465,6 +465,9 @@ static int sharded_impl(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, 
     if (!comm || !y_shards)
         return sdq::set_error_message(SDQ_ERR_INVALID,
                                       "sdq_quantized_matmul_sharded: comm and y_shards must be non-null");
+    if (x_dtype != SDQ_BF16 || sb_dtype != SDQ_BF16 || y_dtype != SDQ_BF16)
+        return sdq::set_error_message(SDQ_ERR_UNSUPPORTED,
+                                      "sdq_quantized_matmul_sharded: x, y, scales and biases must be bf16");
     if (reinterpret_cast<uintptr_t>(y_shards) % 16 != 0 ||
         (y && reinterpret_cast<uintptr_t>(y) % 16 != 0))
         return sdq::set_error_message(SDQ_ERR_INVALID,

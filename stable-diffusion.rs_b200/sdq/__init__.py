@@ -63,10 +63,16 @@ def _need_cuda(*ts):
             raise SdqError(SDQ_ERR_INVALID, "libsdq takes contiguous row-major tensors")
 
 
-def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None):
+def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None,
+             sb_dtype=torch.bfloat16):
     """``mlx_quantize`` replacement: w [n, k] f32/bf16 -> (wq u32 [n, k*bits/32] as int32,
-    scales bf16 [n, k/64], biases bf16 [n, k/64])."""
+    scales [n, k/64], biases [n, k/64]).
+
+    ``sb_dtype`` is bf16 (half the bytes) or f32 (the dtype MLX gives an f32 weight's scales);
+    the values are the same bf16-rounded ones either way, widened exactly when f32."""
     _need_cuda(w)
+    if sb_dtype not in (torch.bfloat16, torch.float32):
+        raise SdqError(SDQ_ERR_UNSUPPORTED, f"scales and biases must be bf16 or f32, not {sb_dtype}")
     if w.dim() != 2:
         raise SdqError(SDQ_ERR_INVALID, f"quantize wants a 2-D weight, got shape {tuple(w.shape)}")
     n, k = w.shape
@@ -76,10 +82,10 @@ def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, strea
         check(lib().sdq_quantize(_ptr(w), _dt(w), n, k, group_size, bits, MODE.encode(), _ptr(dummy),
                                  _ptr(dummy), _ptr(dummy), SDQ_BF16, _stream(stream)))
     wq = torch.empty((n, k * bits // 32), device=w.device, dtype=torch.int32)
-    s = torch.empty((n, k // GROUP_SIZE), device=w.device, dtype=torch.bfloat16)
+    s = torch.empty((n, k // GROUP_SIZE), device=w.device, dtype=sb_dtype)
     b = torch.empty_like(s)
     check(lib().sdq_quantize(_ptr(w), _dt(w), n, k, group_size, bits, MODE.encode(), _ptr(wq), _ptr(s),
-                             _ptr(b), SDQ_BF16, _stream(stream)))
+                             _ptr(b), _DT[sb_dtype], _stream(stream)))
     return wq, s, b
 
 
@@ -100,7 +106,9 @@ def quantized_matmul(x: torch.Tensor, wq, scales, biases, group_size: int = GROU
                      stream=None) -> torch.Tensor:
     """``mlx_quantized_matmul`` replacement (transpose=true): x [..., k] -> [..., n].
 
-    A 3-D ``x`` ([b, s, k]) is flattened to M = b*s rows, as MLX does."""
+    A 3-D ``x`` ([b, s, k]) is flattened to M = b*s rows, as MLX does.  ``x``, the scales and
+    the result may each be bf16 or f32; the result defaults to ``x``'s dtype.  f32 inputs are
+    rounded to bf16 for the tensor cores; an f32 result is the f32 accumulator, unrounded."""
     _need_cuda(x, wq, scales, biases, bias, out)
     lead = x.shape[:-1]
     k = x.shape[-1]
@@ -109,7 +117,8 @@ def quantized_matmul(x: torch.Tensor, wq, scales, biases, group_size: int = GROU
         m *= d
     n = wq.shape[0]
     if out is None:
-        out = torch.empty((*lead, n), device=x.device, dtype=torch.bfloat16)
+        out = torch.empty((*lead, n), device=x.device,
+                          dtype=torch.float32 if x.dtype == torch.float32 else torch.bfloat16)
     check(lib().sdq_quantized_matmul(_ptr(x), _dt(x), m, k, _ptr(wq), _ptr(scales), _ptr(biases),
                                      _dt(scales), n, 1, group_size, bits, MODE.encode(), _ptr(bias),
                                      _ptr(out), _dt(out), _stream(stream)))
@@ -201,6 +210,14 @@ def device_status(stream=None) -> None:
     check(lib().sdq_device_status(_stream(stream)))
 
 
+def debug_wait_hook(wait_limit_ns: int = 0, withhold_first_copy: bool = False, stream=None) -> None:
+    """Testing hook (``sdq_debug_wait_hook``): shorten the kernels' bounded waits to
+    ``wait_limit_ns`` (0 restores 2 s) and, with ``withhold_first_copy``, make every CTA's
+    weight producer skip its first copy so that the abort path runs."""
+    check(lib().sdq_debug_wait_hook(ctypes.c_uint64(wait_limit_ns), int(bool(withhold_first_copy)),
+                                    _stream(stream)))
+
+
 @dataclass
 class QuantizedArray:
     """A weight held quantised at rest (mlx.rs:1846-1854): packed ``weight`` (u32 words,
@@ -215,9 +232,10 @@ class QuantizedArray:
     bits: int
 
     @classmethod
-    def quantize(cls, w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None):
+    def quantize(cls, w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, stream=None,
+                 sb_dtype=torch.bfloat16):
         """``[out, in]`` in, packed ``[out, in * bits / 32]`` out (mlx.rs:1861)."""
-        wq, s, b = quantize(w, group_size, bits, stream)
+        wq, s, b = quantize(w, group_size, bits, stream, sb_dtype)
         return cls(wq, s, b, group_size, bits)
 
     def dequantize(self, out_dtype=torch.bfloat16, stream=None) -> torch.Tensor:

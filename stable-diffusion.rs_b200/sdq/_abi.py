@@ -41,6 +41,7 @@ SIGNATURES = {
     "sdq_gguf_quantize": (_i32, [_p, _i32, _i64, _i64, _i32, _i32, _p, _p, _p, _i32, _p]),
     "sdq_gguf_dequantize": (_i32, [_p, _i32, _i64, _p, _i32, _p]),
     "sdq_device_status": (_i32, [_p]),
+    "sdq_debug_wait_hook": (_i32, [ctypes.c_uint64, _i32, _p]),
     "sdq_comm_unique_id": (_i32, [_p]),
     "sdq_comm_init": (_i32, [_p, _i32, _i32, ctypes.POINTER(ctypes.c_void_p)]),
     "sdq_comm_destroy": (_i32, [_p]),

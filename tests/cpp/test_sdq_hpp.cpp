@@ -74,12 +74,14 @@ int main() {
                 want[r * out + o] = float(acc);
             }
         auto w = must(sdq::Array::from_slice_f32(wv, {(int64_t)out, (int64_t)inp}), "weight");
-        auto x = must(sdq::Array::from_slice_f32(xv, {(int64_t)rows, (int64_t)inp}, SDQ_BF16), "x");
+        // f32 activations, f32 weights, f32 result: the reference's dtypes.
+        auto x = must(sdq::Array::from_slice_f32(xv, {(int64_t)rows, (int64_t)inp}), "x");
         for (size_t bits : {4u, 8u}) {
             auto q = must(sdq::QuantizedArray::quantize(w, 64, bits, s), "quantize");
             auto y = must(q.matmul(x, s), "matmul");
             const double c = cosine(want, must(y.to_vec_f32(s), "to_vec_f32"));
-            check(y.shape() == std::vector<int64_t>{(int64_t)rows, (int64_t)out} && c > 0.999,
+            check(y.shape() == std::vector<int64_t>{(int64_t)rows, (int64_t)out} && y.dtype() == SDQ_F32 &&
+                      q.scales.dtype() == SDQ_F32 && c > 0.999,
                   bits == 4 ? "matmul vs dense 4-bit cosine" : "matmul vs dense 8-bit cosine", c);
         }
     }

@@ -67,7 +67,7 @@ def _qmm(x=1, m=4, k=128, n=64, bits=4, group=64, mode=b"affine", transpose=1, x
     (dict(n=0), _abi.SDQ_ERR_INVALID, "n (rows"),
     (dict(transpose=0), _abi.SDQ_ERR_UNSUPPORTED, "transpose=false"),
     (dict(x=0), _abi.SDQ_ERR_INVALID, "non-null"),
-    (dict(xdt=0), _abi.SDQ_ERR_UNSUPPORTED, "bf16"),
+    (dict(xdt=2), _abi.SDQ_ERR_UNSUPPORTED, "bf16 or f32"),
 ])
 def test_invalid_arguments_are_rejected_with_a_message(kwargs, code, needle):
     assert _qmm(**kwargs) == code
