@@ -29,7 +29,8 @@ launches are replayed as one CUDA graph.  cfg4 and encoders time each step with 
 events after a 256 MiB L2-flushing write.  The total is max-reduced over ranks.  `e2e`
 repeats the step eagerly through the public API with the step's X copied from pinned host
 memory and the (gathered) Y copied back inside the timed region (L2 flushed before each
-step, outside its events).
+step, outside its events); on one GPU that is one sdq_quantized_matmul_host call, which
+overlaps the upload, product and download of row chunks.
 """
 from __future__ import annotations
 
@@ -762,11 +763,11 @@ def main():
         flush.zero_()
         if i >= args.warmup:
             e2e_ev[i - args.warmup][0].record(stream)
-        xd.copy_(xh, non_blocking=True)
         if comm is None:
-            sdq.quantized_matmul(xd, wq, s, b, 64, bits, out=y)
-            yh.copy_(y, non_blocking=True)
+            # One call: upload, product and download of row chunks overlap inside it.
+            sdq.quantized_matmul_host(xh, wq, s, b, 64, bits, out=yh, x_dev=xd, y_dev=y)
         else:
+            xd.copy_(xh, non_blocking=True)
             sdq.quantized_matmul_sharded(xd, wq, s, b, comm, 64, bits, y_shards=y_shards, out=y_full)
             yh.copy_(y_full, non_blocking=True)
         if i >= args.warmup:
@@ -836,8 +837,9 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_step,
                     "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * world * 2,
-                    "path": "sdq.quantized_matmul%s (C ABI) with pinned host X in, Y out" %
-                            ("" if world == 1 else "_sharded")},
+                    "path": ("sdq.quantized_matmul_host (C ABI): pinned host X in, host Y out, row chunks "
+                             "uploaded, multiplied and downloaded in overlap" if world == 1 else
+                             "sdq.quantized_matmul_sharded (C ABI) with pinned host X in, Y out")},
             # N > 1: the overlapped path (M > 8) runs only the tensor-core kernel (the peers'
             # blocks arrive by copy engine into the communicator's output); M <= 8 adds the permute.
             "gpu_launches": args.steps * (1 if world == 1 or m > 8 else 2),

@@ -116,6 +116,27 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                          const char* mode, const void* bias, void* y, sdq_dtype y_dtype,
                          void* stream);
 
+/*
+ * sdq_quantized_matmul with the activations and the result in HOST memory, as
+ * the reference's callers hold them around QuantizedArray::matmul (mlx.rs:
+ * 1952-1975, on MLX's unified memory): x_host [m,k] goes to the device
+ * workspace x_dev, the product into the workspace y_dev, and y_dev back to
+ * y_host [m,n].  The rows go in chunks of chunk_rows (0: automatic -- about
+ * m/8 rows, 128 to 1024; at most 64 chunks) so that one chunk uploads while the
+ * previous one's product runs and the one before downloads: the call costs
+ * about the upload of x plus one chunk's product and download.  Page-locked
+ * host memory (cudaHostAlloc / cudaHostRegister) lets the copies overlap;
+ * pageable memory works, without the overlap.  Asynchronous on `stream` like
+ * the other entry points: y_host is complete once `stream` has caught up.
+ * x_dev holds m*k and y_dev m*n values of x_dtype / y_dtype; the other
+ * arguments are sdq_quantized_matmul's (transpose true, mode "affine").
+ */
+int sdq_quantized_matmul_host(const void* x_host, sdq_dtype x_dtype, int64_t m, int64_t k,
+                              const uint32_t* wq, const void* scales, const void* biases,
+                              sdq_dtype sb_dtype, int64_t n, int group_size, int bits,
+                              const void* bias, void* y_host, sdq_dtype y_dtype, void* x_dev,
+                              void* y_dev, int64_t chunk_rows, void* stream);
+
 /* Activations for sdq_quantized_matmul_epilogue (values fixed; part of the ABI). */
 #define SDQ_ACT_NONE 0
 #define SDQ_ACT_GELU_TANH 1 /* 0.5 a (1 + tanh(sqrt(2/pi) (a + 0.044715 a^3))), mlx.rs:1033-1052 */

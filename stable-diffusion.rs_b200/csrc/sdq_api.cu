@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -161,6 +162,165 @@ int run_qmm(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void*
     }
     return ok();
 }
+
+// sdq_quantized_matmul after its argument checks: the bf16 kernels directly, or, for f32
+// activations or scales, after rounding them to bf16 (nearest even) into stream-ordered
+// temporaries -- the one place the library allocates on the compute path, through the
+// stream's memory pool.  Scales and biases from sdq_quantize are bf16 values already and stay
+// exact; an f32 result is the f32 accumulator.
+int qmm_any_dtype(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
+                  const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n, int bits,
+                  const void* bias, void* y, sdq_dtype y_dtype, cudaStream_t st, const char* fn) {
+    EpiArgs epi = bias_only(bias);
+    epi.f32 = y_dtype == SDQ_F32;
+    if (x_dtype == SDQ_BF16 && sb_dtype == SDQ_BF16)
+        return run_qmm(x, m, k, wq, scales, biases, n, bits, epi, y, st, fn);
+    const size_t xb = x_dtype == SDQ_F32 ? ((size_t)m * k * 2 + 255) & ~(size_t)255 : 0;
+    const size_t sbb = sb_dtype == SDQ_F32 ? ((size_t)n * (k / 64) * 2 + 255) & ~(size_t)255 : 0;
+    uint8_t* tmp = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&tmp), xb + 2 * sbb, st);
+    if (e != cudaSuccess) return fail(SDQ_ERR_CUDA, "%s: cudaMallocAsync (f32 inputs): %s", fn,
+                                      cudaGetErrorString(e));
+    const void* xk = x;
+    const void* sk = scales;
+    const void* bk = biases;
+    if (x_dtype == SDQ_F32) {
+        e = launch_f32_to_bf16(static_cast<const float*>(x), tmp, m * k, st);
+        xk = tmp;
+    }
+    if (e == cudaSuccess && sb_dtype == SDQ_F32) {
+        e = launch_f32_to_bf16(static_cast<const float*>(scales), tmp + xb, n * (k / 64), st);
+        if (e == cudaSuccess) e = launch_f32_to_bf16(static_cast<const float*>(biases), tmp + xb + sbb, n * (k / 64), st);
+        sk = tmp + xb;
+        bk = tmp + xb + sbb;
+    }
+    if (e != cudaSuccess) {
+        cudaFreeAsync(tmp, st);
+        return fail(SDQ_ERR_CUDA, "%s: f32 -> bf16 conversion: %s", fn, cudaGetErrorString(e));
+    }
+    int rc = run_qmm(xk, m, k, wq, sk, bk, n, bits, epi, y, st, fn);
+    e = cudaFreeAsync(tmp, st);
+    if (rc == SDQ_OK && e != cudaSuccess) return fail(SDQ_ERR_CUDA, "%s: cudaFreeAsync: %s", fn,
+                                                      cudaGetErrorString(e));
+    return rc;
+}
+
+// ---------------------------------------------------------------- host-buffer pipeline
+// Each device keeps two copy streams (upload, download) and a ring of events, made once per
+// CUDA context.  A call records an event on the caller's stream; both copy streams wait for
+// it, so the call is ordered after the caller's earlier work on x_dev / y_dev / the host
+// buffers.  Then, per row chunk c: the upload stream copies x rows into x_dev and records
+// up[c]; the caller's stream waits for up[c] and runs the product of those rows into y_dev,
+// recording mm[c]; the download stream waits for mm[c] and copies the rows of y out.  The
+// caller's stream finally waits for the download stream.  Uploads run back to back on one
+// copy engine, downloads on the other (PCIe is full duplex), and each chunk's product runs
+// while later chunks upload, so the call costs about the upload of x plus one chunk's
+// product and download.  The events are re-recorded by the next call; a wait uses the
+// record current when the wait was issued, and the lock keeps calls from interleaving
+// their records and waits.
+constexpr int kPipeChunks = 64;
+struct HostPipe {
+    unsigned long long ctx = 0;
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t start = nullptr, done = nullptr;
+    cudaEvent_t up_ev[kPipeChunks] = {}, mm_ev[kPipeChunks] = {};
+};
+std::mutex g_pipe_mu;
+HostPipe g_pipe[64];
+
+cudaError_t pipe_for_current_device(HostPipe** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    HostPipe& p = g_pipe[dev];
+    const unsigned long long ctx = current_context_id();
+    if (p.up == nullptr || ctx == 0 || p.ctx != ctx) {
+        // A new context (first use, or after a cudaDeviceReset, which destroyed the old
+        // streams and events with their context): make them anew.
+        p = HostPipe{};
+        const unsigned fl = cudaEventDisableTiming;
+        if ((e = cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&p.start, fl)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&p.done, fl)) != cudaSuccess)
+            return e;
+        for (int i = 0; i < kPipeChunks; ++i)
+            if ((e = cudaEventCreateWithFlags(&p.up_ev[i], fl)) != cudaSuccess ||
+                (e = cudaEventCreateWithFlags(&p.mm_ev[i], fl)) != cudaSuccess)
+                return e;
+        p.ctx = ctx;
+    }
+    *out = &p;
+    return cudaSuccess;
+}
+
+// Row counts of the chunks, into rows[kPipeChunks]; returns how many.  Chunks of `asked`
+// rows, or with `asked` = 0 of about m / 8 rows (a multiple of 64, 128 to 1024: a product
+// that still fills the SMs, few enough calls that the host keeps ahead of the copies); more
+// rows when m would need over kPipeChunks chunks.  On a B200 over PCIe 5 (cfg2: 100.7 MB up,
+// 25.2 MB down) 384- and 512-row chunks both took 2.02-2.03 ms, 128-row chunks 2.39 ms;
+// splitting the last chunk into halves and quarters to shorten the tail (2.04 ms) and
+// alternating two upload streams (2.10-2.19 ms) measured slower.
+int pipe_chunks(int64_t m, int64_t asked, int64_t* rows) {
+    int64_t r = asked;
+    if (r <= 0) {
+        r = ((m + 7) / 8 + 63) / 64 * 64;
+        r = r < 128 ? 128 : (r > 1024 ? 1024 : r);
+    }
+    const int64_t floor_rows = (m + kPipeChunks - 1) / kPipeChunks;
+    if (r < floor_rows) r = floor_rows;
+    int n = 0;
+    for (int64_t r0 = 0; r0 < m; r0 += r) rows[n++] = m - r0 < r ? m - r0 : r;
+    return n;
+}
+
+int qmm_host_pipeline(const void* x_host, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
+                      const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n, int bits,
+                      const void* bias, void* y_host, sdq_dtype y_dtype, void* x_dev, void* y_dev,
+                      int64_t chunk_rows, cudaStream_t st, const char* fn) {
+    const size_t xe = x_dtype == SDQ_F32 ? 4 : 2, ye = y_dtype == SDQ_F32 ? 4 : 2;
+    int64_t rows[kPipeChunks];
+    const int nch = pipe_chunks(m, chunk_rows, rows);
+    std::lock_guard<std::mutex> lock(g_pipe_mu);
+    HostPipe* p = nullptr;
+    cudaError_t e = pipe_for_current_device(&p);
+    if (e != cudaSuccess) return fail(SDQ_ERR_CUDA, "%s: copy streams: %s", fn, cudaGetErrorString(e));
+    if ((e = cudaEventRecord(p->start, st)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(p->up, p->start, 0)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(p->down, p->start, 0)) != cudaSuccess)
+        return fail(SDQ_ERR_CUDA, "%s: stream fork: %s", fn, cudaGetErrorString(e));
+    int rc = SDQ_OK;
+    int64_t r0 = 0;
+    for (int c = 0; c < nch && rc == SDQ_OK; r0 += rows[c], ++c) {
+        const int64_t mc = rows[c];
+        uint8_t* xd = static_cast<uint8_t*>(x_dev) + (size_t)r0 * k * xe;
+        uint8_t* yd = static_cast<uint8_t*>(y_dev) + (size_t)r0 * n * ye;
+        e = cudaMemcpyAsync(xd, static_cast<const uint8_t*>(x_host) + (size_t)r0 * k * xe,
+                            (size_t)mc * k * xe, cudaMemcpyHostToDevice, p->up);
+        if (e == cudaSuccess) e = cudaEventRecord(p->up_ev[c], p->up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, p->up_ev[c], 0);
+        if (e != cudaSuccess) { rc = fail(SDQ_ERR_CUDA, "%s: upload: %s", fn, cudaGetErrorString(e)); break; }
+        rc = qmm_any_dtype(xd, x_dtype, mc, k, wq, scales, biases, sb_dtype, n, bits, bias, yd, y_dtype,
+                           st, fn);
+        if (rc != SDQ_OK) break;
+        e = cudaEventRecord(p->mm_ev[c], st);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->mm_ev[c], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<uint8_t*>(y_host) + (size_t)r0 * n * ye, yd, (size_t)mc * n * ye,
+                                cudaMemcpyDeviceToHost, p->down);
+        if (e != cudaSuccess) rc = fail(SDQ_ERR_CUDA, "%s: download: %s", fn, cudaGetErrorString(e));
+    }
+    // Join the copy streams back into the caller's stream, also after a failure, so that
+    // nothing the call enqueued outlives the caller's view of it.
+    cudaError_t j = cudaEventRecord(p->done, p->down);
+    if (j == cudaSuccess) j = cudaStreamWaitEvent(st, p->done, 0);
+    if (j == cudaSuccess) j = cudaEventRecord(p->done, p->up);
+    if (j == cudaSuccess) j = cudaStreamWaitEvent(st, p->done, 0);
+    if (rc != SDQ_OK) return rc;
+    if (j != cudaSuccess) return fail(SDQ_ERR_CUDA, "%s: stream join: %s", fn, cudaGetErrorString(j));
+    return ok();
+}
 }  // namespace sdq
 
 extern "C" {
@@ -236,41 +396,32 @@ int sdq_quantized_matmul(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
     if ((rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, transpose,
                                 group_size, bits, mode, bias, y, y_dtype, fn)))
         return rc;
-    EpiArgs epi = bias_only(bias);
-    epi.f32 = y_dtype == SDQ_F32;
-    if (x_dtype == SDQ_BF16 && sb_dtype == SDQ_BF16)
-        return run_qmm(x, m, k, wq, scales, biases, n, bits, epi, y, stream, fn);
-    // f32 activations or scales: the tensor cores take bf16, so they are rounded (nearest
-    // even) into stream-ordered temporaries first -- the one place the library allocates on
-    // the compute path, through the stream's memory pool.  Scales and biases from
-    // sdq_quantize are bf16 values already and stay exact.
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const size_t xb = x_dtype == SDQ_F32 ? ((size_t)m * k * 2 + 255) & ~(size_t)255 : 0;
-    const size_t sbb = sb_dtype == SDQ_F32 ? ((size_t)n * (k / 64) * 2 + 255) & ~(size_t)255 : 0;
-    uint8_t* tmp = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&tmp), xb + 2 * sbb, st);
-    if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: cudaMallocAsync (f32 inputs)", e);
-    const void* xk = x;
-    const void* sk = scales;
-    const void* bk = biases;
-    if (x_dtype == SDQ_F32) {
-        e = launch_f32_to_bf16(static_cast<const float*>(x), tmp, m * k, st);
-        xk = tmp;
+    return qmm_any_dtype(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n, bits, bias, y, y_dtype,
+                         static_cast<cudaStream_t>(stream), fn);
+}
+
+int sdq_quantized_matmul_host(const void* x_host, sdq_dtype x_dtype, int64_t m, int64_t k,
+                              const uint32_t* wq, const void* scales, const void* biases,
+                              sdq_dtype sb_dtype, int64_t n, int group_size, int bits,
+                              const void* bias, void* y_host, sdq_dtype y_dtype, void* x_dev,
+                              void* y_dev, int64_t chunk_rows, void* stream) {
+    const char* fn = "sdq_quantized_matmul_host";
+    int rc;
+    if (!x_host || !y_host) return fail(SDQ_ERR_INVALID, "%s: x_host and y_host must be non-null", fn);
+    if ((rc = sdq::validate_qmm(x_dev, x_dtype, m, k, wq, scales, biases, sb_dtype, n, 1, group_size,
+                                bits, "affine", bias, y_dev, y_dtype, fn)))
+        return rc;
+    if (chunk_rows < 0) return fail(SDQ_ERR_INVALID, "%s: chunk_rows must be >= 0 (0: automatic)", fn);
+    for (const void* p : {x_host, static_cast<const void*>(y_host)}) {
+        cudaPointerAttributes a{};
+        cudaError_t e = cudaPointerGetAttributes(&a, p);
+        if (e != cudaSuccess) return cuda_fail("sdq_quantized_matmul_host: cudaPointerGetAttributes", e);
+        if (a.type == cudaMemoryTypeDevice)
+            return fail(SDQ_ERR_INVALID,
+                        "%s: x_host / y_host is device memory; call sdq_quantized_matmul instead", fn);
     }
-    if (e == cudaSuccess && sb_dtype == SDQ_F32) {
-        e = launch_f32_to_bf16(static_cast<const float*>(scales), tmp + xb, n * (k / 64), st);
-        if (e == cudaSuccess) e = launch_f32_to_bf16(static_cast<const float*>(biases), tmp + xb + sbb, n * (k / 64), st);
-        sk = tmp + xb;
-        bk = tmp + xb + sbb;
-    }
-    if (e != cudaSuccess) {
-        cudaFreeAsync(tmp, st);
-        return cuda_fail("sdq_quantized_matmul: f32 -> bf16 conversion", e);
-    }
-    rc = run_qmm(xk, m, k, wq, sk, bk, n, bits, epi, y, stream, fn);
-    e = cudaFreeAsync(tmp, st);
-    if (rc == SDQ_OK && e != cudaSuccess) return cuda_fail("sdq_quantized_matmul: cudaFreeAsync", e);
-    return rc;
+    return qmm_host_pipeline(x_host, x_dtype, m, k, wq, scales, biases, sb_dtype, n, bits, bias, y_host,
+                             y_dtype, x_dev, y_dev, chunk_rows, static_cast<cudaStream_t>(stream), fn);
 }
 
 int sdq_quantized_matmul_epilogue(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,

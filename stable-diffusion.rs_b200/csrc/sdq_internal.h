@@ -54,6 +54,10 @@ cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* w
                           const void* scales, const void* biases, int64_t n, int bits,
                           const EpiArgs& epi, void* y, cudaStream_t st, const char** msg);
 
+// The unique id of the calling thread's current CUDA context (0 when the driver cannot say).
+// A cudaDeviceReset replaces the context; caches of per-context objects compare this id.
+unsigned long long current_context_id();
+
 // The argument and device checks of sdq_quantized_matmul (status, message set on failure).
 int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const uint32_t* wq,
                  const void* scales, const void* biases, sdq_dtype sb_dtype, int64_t n,

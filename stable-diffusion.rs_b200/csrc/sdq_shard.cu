@@ -530,6 +530,24 @@ int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, in
 // buffer lives in this file-scope array instead of a caller buffer.  It costs
 // kStaticShardBytes of device memory on every GPU that loads the library, for as
 // long as the process runs, and bounds world * m * n_local.
+namespace sdq {
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+unsigned long long current_context_id() {
+    static CtxGetIdFn get_id = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<CtxGetIdFn>(p);
+        return static_cast<CtxGetIdFn>(nullptr);
+    }();
+    unsigned long long id = 0;
+    if (get_id == nullptr || get_id(nullptr, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+}  // namespace sdq
+
 namespace {
 
 constexpr size_t kStaticShardBytes = size_t(8) << 20;                // 8 MiB
@@ -547,23 +565,6 @@ std::mutex g_static_mu;
 void* g_static_ptr[kMaxDevices] = {};
 unsigned long long g_static_ctx[kMaxDevices] = {};
 
-using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
-
-// The unique id of the calling thread's current context (0 when the driver cannot say).
-unsigned long long current_context_id() {
-    static CtxGetIdFn get_id = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            return reinterpret_cast<CtxGetIdFn>(p);
-        return static_cast<CtxGetIdFn>(nullptr);
-    }();
-    unsigned long long id = 0;
-    if (get_id == nullptr || get_id(nullptr, &id) != CUDA_SUCCESS) return 0;
-    return id;
-}
-
 cudaError_t static_shards_on_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -571,14 +572,14 @@ cudaError_t static_shards_on_current_device(void** out) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     // Id 0: no context is current yet (or the driver cannot tell); the lookup below makes
     // the primary context current, and without an id the address is looked up every call.
-    const unsigned long long ctx = current_context_id();
+    const unsigned long long ctx = sdq::current_context_id();
     std::lock_guard<std::mutex> lock(g_static_mu);
     if (!g_static_ptr[dev] || ctx == 0 || g_static_ctx[dev] != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_static_shards);
         if (e != cudaSuccess) return e;
         g_static_ptr[dev] = p;
-        g_static_ctx[dev] = current_context_id();
+        g_static_ctx[dev] = sdq::current_context_id();
     }
     *out = g_static_ptr[dev];
     return cudaSuccess;

@@ -125,6 +125,41 @@ def quantized_matmul(x: torch.Tensor, wq, scales, biases, group_size: int = GROU
     return out
 
 
+def quantized_matmul_host(x_host: torch.Tensor, wq, scales, biases, group_size: int = GROUP_SIZE,
+                          bits: int = 4, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                          x_dev: torch.Tensor | None = None, y_dev: torch.Tensor | None = None,
+                          chunk_rows: int = 0, stream=None) -> torch.Tensor:
+    """:func:`quantized_matmul` on HOST activations into a HOST result (``sdq_quantized_matmul_host``):
+    the rows go up, through the product and back down in overlapped chunks.  ``x_host`` and
+    ``out`` are CPU tensors (pinned for the copies to overlap); ``x_dev`` / ``y_dev`` are the
+    device workspaces (allocated here when not given).  Asynchronous on ``stream``."""
+    _need_cuda(wq, scales, biases, bias, x_dev, y_dev)
+    if x_host.is_cuda or not x_host.is_contiguous():
+        raise SdqError(SDQ_ERR_INVALID, "x_host must be a contiguous CPU tensor")
+    lead = x_host.shape[:-1]
+    k = x_host.shape[-1]
+    m = 1
+    for d in lead:
+        m *= d
+    n = wq.shape[0]
+    ydt = torch.float32 if x_host.dtype == torch.float32 else torch.bfloat16
+    if out is None:
+        out = torch.empty((*lead, n), dtype=ydt, pin_memory=True)
+    if out.is_cuda or not out.is_contiguous():
+        raise SdqError(SDQ_ERR_INVALID, "out must be a contiguous CPU tensor")
+    dev = wq.device
+    if x_dev is None:
+        x_dev = torch.empty((m, k), device=dev, dtype=x_host.dtype)
+    if y_dev is None:
+        y_dev = torch.empty((m, n), device=dev, dtype=out.dtype)
+    if x_dev.numel() < m * k or y_dev.numel() < m * n or x_dev.dtype != x_host.dtype or y_dev.dtype != out.dtype:
+        raise SdqError(SDQ_ERR_INVALID, "x_dev / y_dev must hold m*k / m*n values of x_host's / out's dtype")
+    check(lib().sdq_quantized_matmul_host(_ptr(x_host), _dt(x_host), m, k, _ptr(wq), _ptr(scales), _ptr(biases),
+                                          _dt(scales), n, group_size, bits, _ptr(bias), _ptr(out), _dt(out),
+                                          _ptr(x_dev), _ptr(y_dev), chunk_rows, _stream(stream)))
+    return out
+
+
 def quantized_matmul_epilogue(x: torch.Tensor, wq, scales, biases, group_size: int = GROUP_SIZE,
                               bits: int = 4, bias: torch.Tensor | None = None, act=None,
                               gate: torch.Tensor | None = None, residual: torch.Tensor | None = None,

@@ -33,6 +33,8 @@ SIGNATURES = {
     "sdq_dequantize": (_i32, [_p, _p, _p, _i32, _i64, _i64, _i32, _i32, ctypes.c_char_p, _p, _i32, _p]),
     "sdq_quantized_matmul": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32, _i32,
                                     ctypes.c_char_p, _p, _p, _i32, _p]),
+    "sdq_quantized_matmul_host": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32, _p, _p,
+                                         _i32, _p, _p, _i64, _p]),
     "sdq_quantized_matmul_epilogue": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _i32, _i64, _i32, _i32,
                                              _p, _i32, _p, _p, _p, _i32, _p]),
     "sdq_resident_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32]),
