@@ -757,6 +757,12 @@ def main():
     xh.copy_(x.cpu())
     yh = torch.empty((m, n * world), dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
+    # N > 1: X and Y cross the host link once per step between them: each rank uploads its
+    # 1/N of X's rows, NCCL gathers X over NVLink, and each rank reads back its 1/N of the
+    # gathered Y's rows (every rank holds the whole Y on the device).
+    split = comm is not None and m % world == 0
+    rows = m // world if split else m
+    xpart = torch.empty((rows, k), device=dev, dtype=torch.bfloat16) if split else None
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
     for i in range(args.warmup + args.steps):
@@ -766,6 +772,11 @@ def main():
         if comm is None:
             # One call: upload, product and download of row chunks overlap inside it.
             sdq.quantized_matmul_host(xh, wq, s, b, 64, bits, out=yh, x_dev=xd, y_dev=y)
+        elif split:
+            xpart.copy_(xh[rank * rows:(rank + 1) * rows], non_blocking=True)
+            dist.all_gather_into_tensor(xd, xpart)
+            sdq.quantized_matmul_sharded(xd, wq, s, b, comm, 64, bits, y_shards=y_shards, out=y_full)
+            yh[rank * rows:(rank + 1) * rows].copy_(y_full[rank * rows:(rank + 1) * rows], non_blocking=True)
         else:
             xd.copy_(xh, non_blocking=True)
             sdq.quantized_matmul_sharded(xd, wq, s, b, comm, 64, bits, y_shards=y_shards, out=y_full)
@@ -836,10 +847,14 @@ def main():
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_step,
-                    "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * world * 2,
+                    "h2d_bytes_per_step": m * k * 2 * (1 if split or world == 1 else world),
+                    "d2h_bytes_per_step": m * n * world * 2 * (1 if split or world == 1 else world),
                     "path": ("sdq.quantized_matmul_host (C ABI): pinned host X in, host Y out, row chunks "
                              "uploaded, multiplied and downloaded in overlap" if world == 1 else
-                             "sdq.quantized_matmul_sharded (C ABI) with pinned host X in, Y out")},
+                             "each rank uploads 1/N of X's rows from pinned host memory, NCCL all-gathers X, "
+                             "sdq.quantized_matmul_sharded (C ABI), each rank reads back 1/N of the gathered "
+                             "Y's rows; bytes are the job's totals" if split else
+                             "sdq.quantized_matmul_sharded (C ABI) with pinned host X in, Y out on every rank")},
             # N > 1: the overlapped path (M > 8) runs only the tensor-core kernel (the peers'
             # blocks arrive by copy engine into the communicator's output); M <= 8 adds the permute.
             "gpu_launches": args.steps * (1 if world == 1 or m > 8 else 2),

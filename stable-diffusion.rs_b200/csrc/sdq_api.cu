@@ -541,16 +541,18 @@ int sdq_debug_wait_hook(uint64_t wait_limit_ns, int withhold_first_copy, void* s
 int sdq_device_status(void* stream) {
     int rc;
     if ((rc = check_device())) return rc;
-    unsigned int st = 0, sv = 0;
+    unsigned int st = 0, sv = 0, ss = 0;
     cudaError_t e = read_and_clear_status(&st, static_cast<cudaStream_t>(stream));
     if (e == cudaSuccess) e = read_and_clear_qmv_status(&sv, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = read_and_clear_shard_status(&ss, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail("sdq_device_status", e);
-    if (st != 0 || sv != 0) {
+    if (st != 0 || sv != 0 || ss != 0) {
         return fail(SDQ_ERR_TIMEOUT,
                     "a device-side wait gave up (tensor-core kernel bits 0x%x: 1 producer, 2 MMA, "
                     "4 dequant, 8 epilogue; small-M kernel bits 0x%x: 1 producer, 2 activations, "
-                    "4 weights); the kernel returned early and its output is incomplete",
-                    st, sv);
+                    "4 weights; sharded exchange bits 0x%x: 1 a peer's pushes never landed); the "
+                    "kernel returned early and its output is incomplete",
+                    st, sv, ss);
     }
     return ok();
 }

@@ -98,6 +98,8 @@ cudaError_t launch_seeded_normals(uint64_t seed, int64_t count, float* out, cuda
 // Device status words of the two matmul kernels (see sdq_ptx.cuh): read, then cleared.
 cudaError_t read_and_clear_status(unsigned int* out, cudaStream_t st);
 cudaError_t read_and_clear_qmv_status(unsigned int* out, cudaStream_t st);
+// Status word of the sharded linear's landed-flag wait (sdq_shard.cu): read, then cleared.
+cudaError_t read_and_clear_shard_status(unsigned int* out, cudaStream_t st);
 // Testing hooks of the two matmul files (wait limit, withheld first copy); synchronise `st`.
 cudaError_t set_wait_hook_tc(unsigned long long limit_ns, int withhold, cudaStream_t st);
 cudaError_t set_wait_hook_qmv(unsigned long long limit_ns, int withhold, cudaStream_t st);

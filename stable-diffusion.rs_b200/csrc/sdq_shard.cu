@@ -13,15 +13,19 @@
 // stream per peer waits on each chunk's count (cuStreamWaitValue32) and copies that
 // chunk's rows of the column block, as one 2-D copy on the copy engines, into the
 // same place of the peer's buffer over NVLink while the kernel computes the next
-// chunk.  A small NCCL all-reduce then tells each rank that every push into its
-// buffer has landed: the buffer holds [m, n], and is copied to the caller's y unless y
-// is that buffer (sdq_comm_output).  (NCCL's send / receive kernels did not start
-// until the compute kernel had finished, so they could not overlap it.)  A kernel that
-// gives up raises every count to its maximum, so no push stream waits for ever.  The
-// buffer is allocated on first use and grows collectively (every rank calls with the
-// same shapes); a second all-reduce at the start of each call, entered once the
-// caller's stream has drained, keeps a fast rank from pushing into a buffer whose
-// previous contents a slower rank is still reading.
+// chunk.  The ranks synchronise through flag words, IPC-mapped like the buffers, that
+// carry a per-call epoch and need no SM: once the caller's stream has drained, a
+// stream write (cuStreamWriteValue32) tells every peer that this rank's buffer may be
+// written, and each push stream waits for its peer's word (cuStreamWaitValue32) before
+// its first copy; after its last copy it writes the peer's "landed" word, and a
+// one-thread kernel waits (acquire loads at system scope, bounded) until every peer's
+// landed word holds the epoch.  Then the buffer holds [m, n], and is copied to the
+// caller's y unless y is that buffer (sdq_comm_output).  (NCCL's send / receive kernels,
+// and NCCL barrier kernels of more than one block, did not start until the compute
+// kernel had finished, so they could not overlap it.)  A kernel that gives up raises
+// every count to its maximum, so no push stream waits for ever on a count.  The buffer
+// is allocated on first use and grows collectively (every rank calls with the same
+// shapes).
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -52,13 +56,20 @@ struct Comm {
     int device = 0;
     // Overlapped exchange (set up when world > 1; the plain path runs without it).
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_bar = nullptr, ev_entry = nullptr,
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_entry = nullptr,
                 ev_kernel = nullptr;
     // One push stream per peer, so that the pushes to different peers run concurrently
     // on different copy engines (one stream runs its copies one after another).
     cudaStream_t push[kMaxWorld] = {};
     cudaEvent_t push_done[kMaxWorld] = {};
-    uint32_t* counters = nullptr;          // kMaxChunks completion counts + 1 barrier word
+    uint32_t* counters = nullptr;          // kMaxChunks completion counts
+    // Barrier words: this rank's [2][kMaxWorld], IPC-exported.  [0][p] receives peer p's
+    // "ready" epoch (p's output may be written: its readers are done), [1][p] its "landed"
+    // epoch (p's pushes into this rank's output are complete).  peer_flags[p] is peer p's
+    // array as mapped here.  The epoch counts overlapped calls; every rank makes the same.
+    uint32_t* flags = nullptr;
+    uint32_t* peer_flags[kMaxWorld] = {};
+    uint32_t epoch = 0;
     // The symmetric output: this rank's [m, n] bf16 buffer, into whose column blocks the
     // kernel and the peers write, and the peers' buffers as mapped here.
     void* xbuf = nullptr;
@@ -92,6 +103,76 @@ ValueFn driver_value_fn(const char* name) {
 ValueFn wait_value_fn() {
     static ValueFn fn = driver_value_fn("cuStreamWaitValue32");
     return fn;
+}
+ValueFn write_value_fn() {
+    static ValueFn fn = driver_value_fn("cuStreamWriteValue32");
+    return fn;
+}
+
+// Status word of the landed-flag wait (read and cleared by sdq_device_status).
+__device__ unsigned int g_shard_status = 0;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// One thread per peer waits until the peer's landed word has reached `epoch` (a cyclic
+// comparison, as CU_STREAM_WAIT_VALUE_GEQ makes), reading it with acquire semantics at
+// system scope: the peer wrote it after its copies into this rank's output, with the
+// memory fence a stream write carries, so the work after this kernel sees those copies.
+// Gives up after 2 s (bit 1 of the status word; the output is then incomplete).
+__global__ void wait_landed(const uint32_t* __restrict__ landed, int world, int rank, uint32_t epoch) {
+    const int p = threadIdx.x;
+    if (p >= world || p == rank) return;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(landed + p) : "memory");
+        if (static_cast<int32_t>(v - epoch) >= 0) return;
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            atomicOr(&g_shard_status, 1u);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+// Allocate this rank's barrier words, export them, and map every peer's (collective).
+bool setup_flags(Comm* c) {
+    const size_t bytes = 2 * kMaxWorld * sizeof(uint32_t);
+    if (cudaMalloc(reinterpret_cast<void**>(&c->flags), bytes) != cudaSuccess) return false;
+    cudaIpcMemHandle_t mine;
+    if (cudaMemset(c->flags, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&mine, c->flags) != cudaSuccess ||
+        cudaMemcpyAsync(c->handles_dev + c->rank, &mine, sizeof mine, cudaMemcpyHostToDevice, c->side) !=
+            cudaSuccess)
+        return false;
+    if (ncclAllGather(c->handles_dev + c->rank, c->handles_dev, sizeof(cudaIpcMemHandle_t), ncclUint8, c->nccl,
+                      c->side) != ncclSuccess)
+        return false;
+    std::vector<cudaIpcMemHandle_t> all(c->world);
+    if (cudaMemcpyAsync(all.data(), c->handles_dev, c->world * sizeof(cudaIpcMemHandle_t), cudaMemcpyDeviceToHost,
+                        c->side) != cudaSuccess ||
+        cudaStreamSynchronize(c->side) != cudaSuccess)
+        return false;
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        void* q = nullptr;
+        if (cudaIpcOpenMemHandle(&q, all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return false;
+        c->peer_flags[p] = static_cast<uint32_t*>(q);
+    }
+    return true;
+}
+
+void release_flags(Comm* c) {
+    for (int p = 0; p < kMaxWorld; ++p)
+        if (c->peer_flags[p]) {
+            cudaIpcCloseMemHandle(c->peer_flags[p]);
+            c->peer_flags[p] = nullptr;
+        }
+    if (c->flags) cudaFree(c->flags);
+    c->flags = nullptr;
 }
 
 
@@ -140,6 +221,18 @@ cudaError_t launch_permute(const void* shards, void* y, int64_t m, int64_t m0, i
 }
 
 }  // namespace
+
+cudaError_t read_and_clear_shard_status(unsigned int* out, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_shard_status, sizeof(unsigned int), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && *out != 0) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_shard_status, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    return e;
+}
 }  // namespace sdq
 
 using namespace sdq;
@@ -156,12 +249,6 @@ static int nccl_fail(const char* what, ncclResult_t r) {
 }
 
 constexpr int kNotOverlapped = -1;
-
-// A zero-byte-payload barrier over the communicator on `st`: an all-reduce of one word.
-static ncclResult_t side_barrier(Comm* c, cudaStream_t st) {
-    uint32_t* w = c->counters + kMaxChunks;
-    return ncclAllReduce(w, w, 1, ncclUint32, ncclMax, c->nccl, st);
-}
 
 // Make this rank's exchange buffer hold `bytes` and map every peer's (collective: all ranks
 // call it with the same size).  Allocates only when the buffer must grow.
@@ -240,10 +327,10 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
                                bits, "affine", bias_local, y, y_dtype, fn);
     if (rc != SDQ_OK) return rc;
     if ((n_local * 2) % 16 != 0) return kNotOverlapped;   // 2-D pushes want 16-byte rows
-    // The start barrier's NCCL kernel is enqueued as the compute kernel starts; the compute
-    // kernel keeps one SM free for it (a persistent kernel on every SM would hold the
-    // barrier, and every push behind it, until the compute had finished).
-    const int grid_cap = sdq::num_sms() - 1;
+    const ValueFn wait = wait_value_fn(), write = write_value_fn();
+    if (wait == nullptr || write == nullptr || c->flags == nullptr) return kNotOverlapped;
+    // The compute kernel takes every SM: the barriers below need none.
+    const int grid_cap = sdq::num_sms();
     const int64_t bt = sdq::qmm_tc_tile_tokens(m, k, n_local, bits, grid_cap);
     const int64_t ntt = (m + bt - 1) / bt;
     if (ntt < 2) return kNotOverlapped;
@@ -262,24 +349,31 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         t_shard_msg = std::string(fn) + ": " + what + ": " + cudaGetErrorString(e);
         return sdq::set_error_message(SDQ_ERR_CUDA, t_shard_msg.c_str());
     };
-    const ValueFn wait = wait_value_fn();
+    const uint32_t epoch = ++c->epoch;
     // The side stream first waits for everything already on the caller's stream (a reader
-    // of the previous result in the symmetric output among it); then one barrier, after
-    // which no rank is still reading its output when the peers start pushing into it.
+    // of the previous result in the symmetric output among it), then tells every peer that
+    // this rank's output may be written.
     cudaError_t e = cudaEventRecord(c->ev_entry, st);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->ev_entry, 0);
     if (e != cudaSuccess) return cuda_err("stream set-up", e);
-    ncclResult_t r = side_barrier(c, c->side);
-    if (r != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        if (write(reinterpret_cast<CUstream>(c->side), reinterpret_cast<CUdeviceptr>(c->peer_flags[p] + c->rank),
+                  epoch, 0) != CUDA_SUCCESS)
+            return cuda_err("ready flag", cudaErrorUnknown);
+    }
     // The kernel needs no barrier: the previous call's copy out of this rank's output was
-    // joined into the caller's stream.  The pushes follow the barrier and the counters' reset.
-    e = cudaEventRecord(c->ev_bar, c->side);
-    if (e == cudaSuccess) e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
+    // joined into the caller's stream.  Each push stream follows the counters' reset and
+    // its peer's ready word.
+    e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = cudaEventRecord(c->ev_start, st);
     for (int p = 0; e == cudaSuccess && p < c->world; ++p) {
         if (p == c->rank) continue;
-        e = cudaStreamWaitEvent(c->push[p], c->ev_bar, 0);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0);
+        e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0);
+        if (e == cudaSuccess &&
+            wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->flags + p), epoch,
+                 0 /* GEQ */) != CUDA_SUCCESS)
+            e = cudaErrorUnknown;
     }
     if (e != cudaSuccess) return cuda_err("stream set-up", e);
     // The kernel writes this rank's block straight into its column block of the output.
@@ -294,13 +388,6 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         }
         return cuda_err("tensor-core kernel", e);
     }
-    // Without stream memory operations every push waits for the whole kernel instead.
-    if (wait == nullptr) {
-        if ((e = cudaEventRecord(c->ev_start, st)) != cudaSuccess) return cuda_err("stream wait", e);
-        for (int p = 0; p < c->world; ++p)
-            if (p != c->rank && (e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0)) != cudaSuccess)
-                return cuda_err("stream wait", e);
-    }
     // Each finished chunk of rows goes, as one 2-D copy, into the same rows and column
     // block of every peer's output.
     const size_t pitch = static_cast<size_t>(ldy) * sizeof(uint16_t);
@@ -311,8 +398,7 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         const size_t off = static_cast<size_t>(m0) * ldy + static_cast<size_t>(c->rank) * n_local;
         for (int p = 0; p < c->world; ++p) {
             if (p == c->rank) continue;
-            if (wait != nullptr &&
-                wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->counters + i),
+            if (wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->counters + i),
                      target, 0 /* GEQ */) != CUDA_SUCCESS)
                 return cuda_err("stream wait on a chunk count", cudaErrorUnknown);
             uint16_t* dst = static_cast<uint16_t*>(c->peer_xbuf[p]) + off;
@@ -322,8 +408,14 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
                 return cuda_err("push to a peer", e);
         }
     }
+    // After its last copy each push stream writes its peer's landed word (the stream write's
+    // memory fence orders it after the copies); the side stream joins the push streams, so
+    // that the next call's kernel does not overwrite this rank's block before it is read.
     for (int p = 0; p < c->world; ++p) {
         if (p == c->rank) continue;
+        if (write(reinterpret_cast<CUstream>(c->push[p]),
+                  reinterpret_cast<CUdeviceptr>(c->peer_flags[p] + kMaxWorld + c->rank), epoch, 0) != CUDA_SUCCESS)
+            return cuda_err("landed flag", cudaErrorUnknown);
         if ((e = cudaEventRecord(c->push_done[p], c->push[p])) != cudaSuccess ||
             (e = cudaStreamWaitEvent(c->side, c->push_done[p], 0)) != cudaSuccess)
             return cuda_err("push join", e);
@@ -332,8 +424,10 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     if ((e = cudaEventRecord(c->ev_kernel, st)) != cudaSuccess ||
         (e = cudaStreamWaitEvent(c->side, c->ev_kernel, 0)) != cudaSuccess)
         return cuda_err("stream join", e);
-    // Every push into this rank's output has landed once every rank has passed here.
-    if ((r = side_barrier(c, c->side)) != ncclSuccess) return nccl_fail("ncclAllReduce (barrier)", r);
+    // Every peer's pushes into this rank's output have landed once its landed word holds
+    // the epoch.
+    wait_landed<<<1, kMaxWorld, 0, c->side>>>(c->flags + kMaxWorld, c->world, c->rank, epoch);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_err("landed wait", e);
     if (y != out) {
         const int threads = 256;
         const bool v8 = (reinterpret_cast<uintptr_t>(y) % 16) == 0 && total % 8 == 0;
@@ -386,10 +480,9 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
                    cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->ev_bar, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_entry, cudaEventDisableTiming) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->ev_kernel, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaMalloc(reinterpret_cast<void**>(&c->counters), (kMaxChunks + 1) * sizeof(uint32_t)) ==
+                   cudaMalloc(reinterpret_cast<void**>(&c->counters), kMaxChunks * sizeof(uint32_t)) ==
                        cudaSuccess &&
                    world <= kMaxWorld &&
                    cudaMalloc(reinterpret_cast<void**>(&c->handles_dev), world * sizeof(cudaIpcMemHandle_t)) ==
@@ -398,10 +491,12 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
             okr = p == rank ||
                   (cudaStreamCreateWithFlags(&c->push[p], cudaStreamNonBlocking) == cudaSuccess &&
                    cudaEventCreateWithFlags(&c->push_done[p], cudaEventDisableTiming) == cudaSuccess);
+        okr = okr && wait_value_fn() != nullptr && write_value_fn() != nullptr && setup_flags(c);
         if (!okr) {
             cudaGetLastError();
+            release_flags(c);
             destroy_push_streams(c);
-            for (cudaEvent_t* ev : {&c->ev_bar, &c->ev_entry, &c->ev_kernel}) {
+            for (cudaEvent_t* ev : {&c->ev_entry, &c->ev_kernel}) {
                 if (*ev) cudaEventDestroy(*ev);
                 *ev = nullptr;
             }
@@ -439,10 +534,10 @@ int sdq_comm_destroy(void* comm) {
         for (int p = 0; p < c->world; ++p)
             if (c->peer_xbuf[p]) cudaIpcCloseMemHandle(c->peer_xbuf[p]);
         if (c->xbuf) cudaFree(c->xbuf);
+        release_flags(c);
         cudaFree(c->handles_dev);
         cudaFree(c->counters);
         destroy_push_streams(c);
-        cudaEventDestroy(c->ev_bar);
         cudaEventDestroy(c->ev_entry);
         cudaEventDestroy(c->ev_kernel);
         cudaEventDestroy(c->ev_end);
