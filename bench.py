@@ -838,7 +838,7 @@ def main():
             "config": {"workload": wl, "descr": DESCR[wl], "M": m, "K": k, "N_per_rank": n, "bits": bits,
                        "group_size": 64, "global_N": n * world,
                        "parallelism": "single GPU" if world == 1 else
-                           f"N-sharded x{world}; output blocks pushed by copy engines over NVLink during the compute",
+                           f"N-sharded x{world}; the kernel's epilogue stores each output tile into every peer's output over NVLink",
                        "l2": f"inputs larger than L2: steps rotate over {rot} copies of X, W, scales, "
                              f"biases and Y ({rot * set_bytes / 1e6:.0f} MB, L2 {L2_BYTES / 1e6:.0f} MB), "
                              "back to back between one event pair"
@@ -855,9 +855,10 @@ def main():
                              "sdq.quantized_matmul_sharded (C ABI), each rank reads back 1/N of the gathered "
                              "Y's rows; bytes are the job's totals" if split else
                              "sdq.quantized_matmul_sharded (C ABI) with pinned host X in, Y out on every rank")},
-            # N > 1: the overlapped path (M > 8) runs only the tensor-core kernel (the peers'
-            # blocks arrive by copy engine into the communicator's output); M <= 8 adds the permute.
-            "gpu_launches": args.steps * (1 if world == 1 or m > 8 else 2),
+            # N > 1: the fused path (M > 8) runs the tensor-core kernel, which also stores its
+            # tiles into the peers' outputs, and the one-thread wait for the peers' tiles;
+            # M <= 8 runs the small-M kernel and the permute (plus NCCL's all-gather).
+            "gpu_launches": args.steps * (1 if world == 1 else 2),
             "clocks": clk.summary(),
         }
         if secondary is not None:

@@ -269,13 +269,16 @@ int sdq_comm_destroy(void* comm);
  * permutes that into y[m, world*n_local].  y_shards is caller-provided
  * (world*m*n_local elements, 16-byte aligned).  The compute step is
  * sdq_quantized_matmul; the exchange is one ncclAllGather on `stream`.
- * When y is non-NULL, world > 1, n_local % 8 == 0 and M spans several token
- * tiles, the exchange instead overlaps the compute: the kernel writes this
- * rank's column block of the communicator's output buffer (see
- * sdq_comm_output) and the copy engines push finished row chunks of it into
- * the same place of every peer's buffer; the assembled [m, world*n_local] is
- * then copied to y, unless y is that buffer.  y_shards is not written on this
- * path.  Every rank must make the same calls, in the same order.
+ * When y is non-NULL, 2 <= world <= 8, n_local % 8 == 0 and m > 8, the
+ * exchange is instead fused into the compute: the tensor-core kernel writes
+ * this rank's column block of the communicator's output buffer (see
+ * sdq_comm_output) and stores each finished output tile at the same place of
+ * every peer's buffer over NVLink; flag words in IPC-mapped memory, written and
+ * waited on by stream memory operations, order the calls across ranks without
+ * using an SM.  The assembled [m, world*n_local] is then copied to y, unless y
+ * is that buffer.  y_shards is not written on this path.  Every rank must make
+ * the same calls, in the same order; a rank that never makes its call leaves
+ * the others' streams waiting, as an NCCL collective would.
  */
 int sdq_quantized_matmul_sharded(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                                  const uint32_t* wq, const void* scales, const void* biases,

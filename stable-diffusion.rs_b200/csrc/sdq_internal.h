@@ -17,6 +17,9 @@ int num_sms();
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
+// Peers one tensor-core kernel can store its output tiles to (one 8-GPU node).
+constexpr int kTcMaxPeers = 7;
+
 // Opt-in dynamic shared memory per block on sm_100 (227 KB).
 constexpr size_t kQmvMaxSmem = 232448;
 
@@ -64,16 +67,18 @@ int validate_qmm(const void* x, sdq_dtype x_dtype, int64_t m, int64_t k, const u
                  int transpose, int& group_size, int& bits, const char* mode, const void* bias,
                  const void* y, sdq_dtype y_dtype, const char* fn);
 
-// The tensor-core matmul for the overlapped sharded linear: the same kernel, on at most
-// grid_cap CTAs (0: every SM), writing rows ldy elements apart and adding 1 to
-// done[tt / chunk_tts] once token tile tt's output tile is in global memory (nchunks
-// counters).  qmm_tc_tile_tokens is the token-tile height the dispatcher picks for the shape.
+// The tensor-core matmul of the overlapped sharded linear: the same kernel, on at most
+// grid_cap CTAs (0: every SM), writing rows ldy elements apart, whose epilogue also stores
+// every output tile at the same place of each of the npeers (<= kTcMaxPeers) peers' copies
+// (peers[i]: this rank's column block in peer i's output) and, once a CTA is done, adds 1
+// to the word landed[i] in peer i's memory.  *grid_out receives the CTA count.
+// qmm_tc_tile_tokens is the token-tile height the dispatcher picks for the shape.
 int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap);
-cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
-                                 const void* scales, const void* biases, int64_t n, int bits,
-                                 const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
-                                 const char** msg, uint32_t* done, int chunk_tts, int nchunks,
-                                 int grid_cap);
+cudaError_t launch_qmm_tc_push(const void* x, int64_t m, int64_t k, const uint32_t* wq,
+                               const void* scales, const void* biases, int64_t n, int bits,
+                               const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
+                               const char** msg, uint16_t* const* peers, uint32_t* const* landed,
+                               int npeers, int grid_cap, int* grid_out);
 
 // Small-M quantised matmul (1 <= M <= 8; TMA weight stream, register-fed m16n8k16 MMAs,
 // programmatic dependent launch).  Sets *taken = false, launching nothing, for what it does

@@ -75,13 +75,19 @@ __host__ __device__ constexpr int tc_threads(int bits) { return 32 * (first_epi_
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 struct TcCfg;
 
-// Optional completion signal for overlapping the output's exchange with the compute:
-// token tile tt belongs to chunk tt / chunk_tts, and once a tile's Y is in global memory
-// the epilogue adds 1 to done[chunk].  done == nullptr turns it off.
+// The exchange of a column-sharded output, fused into the epilogue (npeers > 0): besides
+// this rank's copy, each finished output tile is stored at the same place of every peer's
+// copy of the [M, world * N] output (peer[i] points at this rank's column block there,
+// rows ldy elements apart, over NVLink).  When a CTA has finished its tiles it adds 1 to
+// landed[i], a word in peer i's memory, after a system-scope fence, so a peer that has
+// counted every CTA of every sender sees the whole output.  A CTA that gave up counts
+// too (the status word carries the error), so no peer waits for it.  grid_out (host side
+// only) receives the number of CTAs launched.
 struct TcSignal {
-    uint32_t* done;
-    int chunk_tts;
-    int nchunks;
+    int npeers = 0;
+    uint16_t* peer[kTcMaxPeers] = {};
+    uint32_t* landed[kTcMaxPeers] = {};
+    int* grid_out = nullptr;
 };
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
@@ -482,22 +488,44 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                     for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * ldy + f] = yrow[r * C::BF];
                 }
             }
-            if (sig.done != nullptr) {
-                // This tile's Y must be in global memory before its chunk counts it.
-                if (y_tma) {
-                    if (leader) {
-                        bulk_wait_group0();
-                        __threadfence();
-                        atomicAdd(sig.done + tt / sig.chunk_tts, 1u);
+            if constexpr (!YF32) {
+                if (sig.npeers > 0) {
+                    // The staged tile, 16 bytes per thread and store, into every peer's copy
+                    // (rows past M and pieces past N are not stored; N % 8 == 0).
+                    constexpr int PR = C::BF / 8;                 // 16-byte pieces per row
+                    for (int c = e; c < NCH; c += kEpiGroups) {
+                        const int t0 = tt * BT + c * CW;
+                        const uint8_t* src = sY + (size_t)c * CW * C::BF * 2;
+                        for (int pc = fl; pc < CW * PR; pc += 128) {
+                            const int r = pc / PR, q = pc - r * PR;
+                            const int t = t0 + r, f8 = ft * C::BF + 8 * q;
+                            if (t < M && f8 < N) {
+                                const uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)r * C::BF * 2 + 16 * q);
+                                const size_t off = (size_t)t * ldy + f8;
+#pragma unroll
+                                for (int i = 0; i < kTcMaxPeers; ++i)
+                                    if (i < sig.npeers) *reinterpret_cast<uint4*>(sig.peer[i] + off) = v;
+                            }
+                        }
                     }
-                } else {
-                    __threadfence();
-                    named_barrier_sync(1 + e, 128);
-                    if (leader) atomicAdd(sig.done + tt / sig.chunk_tts, 1u);
                 }
             }
         }
         if (leader && y_tma) bulk_wait_group0();
+        if (sig.npeers > 0) {
+            // Every store of this CTA into the peers' copies is visible before their landed
+            // words count the CTA: each thread's fence orders its stores before the group
+            // barrier, and the leader releases at system scope after it.
+            __threadfence_system();
+            named_barrier_sync(1 + e, 128);
+            if (leader) {
+                __threadfence_system();
+#pragma unroll
+                for (int i = 0; i < kTcMaxPeers; ++i)
+                    if (i < sig.npeers)
+                        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(sig.landed[i]) : "memory");
+            }
+        }
     }
 
     tc_fence_before();
@@ -506,11 +534,6 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
-    }
-    // A CTA that gave up raises every chunk to its maximum, so that nothing waiting
-    // on a count is left waiting (the status word carries the error).
-    if (threadIdx.x == 0 && sig.done != nullptr && *abort_flag) {
-        for (int i = 0; i < sig.nchunks; ++i) atomicMax(sig.done + i, 0x7FFFFFFFu);
     }
 }
 
@@ -609,6 +632,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     const int64_t tiles = ((n + 127) / 128) * ((m + BT - 1) / BT);
     const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
     const int grid = (int)(tiles < cap ? tiles : cap);
+    if (sig.grid_out) *sig.grid_out = grid;
     qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
@@ -698,7 +722,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 cudaError_t launch_qmm_tc(const void* x, int64_t m, int64_t k, const uint32_t* wq,
                           const void* scales, const void* biases, int64_t n, int bits,
                           const EpiArgs& epi, void* y, cudaStream_t st, const char** msg) {
-    const TcSignal off{nullptr, 1, 0};
+    const TcSignal off{};
     return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, n, st, msg, off, 0)
                      : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, n, st, msg, off, 0);
 }
@@ -708,12 +732,19 @@ int qmm_tc_tile_tokens(int64_t m, int64_t k, int64_t n, int bits, int grid_cap) 
     return t == 0 ? 16 : t;
 }
 
-cudaError_t launch_qmm_tc_signal(const void* x, int64_t m, int64_t k, const uint32_t* wq,
-                                 const void* scales, const void* biases, int64_t n, int bits,
-                                 const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
-                                 const char** msg, uint32_t* done, int chunk_tts, int nchunks,
-                                 int grid_cap) {
-    const TcSignal sig{done, chunk_tts, nchunks};
+cudaError_t launch_qmm_tc_push(const void* x, int64_t m, int64_t k, const uint32_t* wq,
+                               const void* scales, const void* biases, int64_t n, int bits,
+                               const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
+                               const char** msg, uint16_t* const* peers, uint32_t* const* landed,
+                               int npeers, int grid_cap, int* grid_out) {
+    if (npeers < 0 || npeers > kTcMaxPeers) return cudaErrorInvalidValue;
+    TcSignal sig{};
+    sig.npeers = npeers;
+    for (int i = 0; i < npeers; ++i) {
+        sig.peer[i] = peers[i];
+        sig.landed[i] = landed[i];
+    }
+    sig.grid_out = grid_out;
     return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap)
                      : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
 }

@@ -5,27 +5,25 @@
 // exchanged over NVLink / NVSwitch into [world, m, n_local] on every rank; a
 // permute kernel turns that into [m, n].
 //
-// When the output is wanted as [m, n] on two or more ranks and M spans several
-// token tiles, the exchange overlaps the compute and uses no SMs.  Every rank owns a
-// symmetric output buffer ([m, n] bf16, IPC-mapped on every peer).  The tensor-core
-// kernel writes this rank's column block of it in place (rows world * n_local apart)
-// and counts, per chunk of token tiles, the output tiles it has finished; one push
-// stream per peer waits on each chunk's count (cuStreamWaitValue32) and copies that
-// chunk's rows of the column block, as one 2-D copy on the copy engines, into the
-// same place of the peer's buffer over NVLink while the kernel computes the next
-// chunk.  The ranks synchronise through flag words, IPC-mapped like the buffers, that
-// carry a per-call epoch and need no SM: once the caller's stream has drained, a
-// stream write (cuStreamWriteValue32) tells every peer that this rank's buffer may be
-// written, and each push stream waits for its peer's word (cuStreamWaitValue32) before
-// its first copy; after its last copy it writes the peer's "landed" word, and a
-// one-thread kernel waits (acquire loads at system scope, bounded) until every peer's
-// landed word holds the epoch.  Then the buffer holds [m, n], and is copied to the
-// caller's y unless y is that buffer (sdq_comm_output).  (NCCL's send / receive kernels,
-// and NCCL barrier kernels of more than one block, did not start until the compute
-// kernel had finished, so they could not overlap it.)  A kernel that gives up raises
-// every count to its maximum, so no push stream waits for ever on a count.  The buffer
-// is allocated on first use and grows collectively (every rank calls with the same
-// shapes).
+// When the output is wanted as [m, n] on two to eight ranks and M > 8, the exchange is
+// fused into the compute kernel.  Every rank owns a symmetric output buffer ([m, n]
+// bf16, IPC-mapped on every peer).  The tensor-core kernel writes this rank's column
+// block of it in place (rows world * n_local apart) and, as each output tile is staged in
+// shared memory, also stores it (16-byte stores over NVLink) at the same place of every
+// peer's buffer, so the exchange runs tile by tile beside the math and uses no copy
+// engine.  The ranks synchronise through flag words, IPC-mapped like the buffers, that
+// need no SM: once the caller's stream has drained, a stream write (cuStreamWriteValue32)
+// tells every peer that this rank's buffer may be written, and the kernel is preceded by
+// stream waits (cuStreamWaitValue32) for every peer's word.  Each CTA, when done, fences
+// at system scope and adds 1 to a count in every peer's memory; a one-thread kernel then
+// waits (acquire loads at system scope, bounded) until every peer's count has grown by
+// the peers' CTA count, after which the buffer holds [m, n] and is copied to the caller's
+// y unless y is that buffer (sdq_comm_output).  Earlier forms of this path pushed
+// finished chunks of rows with the copy engines (one stream per peer) behind NCCL
+// barrier all-reduces; at eight ranks the copies reached about 300 GB/s per GPU and the
+// barrier kernels waited for the compute kernel's SMs.  A kernel that gives up still
+// counts, so no peer waits for it beyond its bound.  The buffer is allocated on first use
+// and grows collectively (every rank calls with the same shapes).
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -45,8 +43,6 @@ namespace {
 
 thread_local std::string t_shard_msg;
 
-constexpr int kMaxChunks = 16;     // chunk counters per communicator
-constexpr int kChunks = 8;         // chunks the overlapped path aims for
 constexpr int kMaxWorld = 64;
 
 struct Comm {
@@ -54,22 +50,18 @@ struct Comm {
     int rank = 0;
     int world = 1;
     int device = 0;
-    // Overlapped exchange (set up when world > 1; the plain path runs without it).
+    // Overlapped exchange (set up when world > 1; the plain path runs without it).  The side
+    // stream carries the collective set-up (handle exchanges); the calls run on the caller's.
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_entry = nullptr,
-                ev_kernel = nullptr;
-    // One push stream per peer, so that the pushes to different peers run concurrently
-    // on different copy engines (one stream runs its copies one after another).
-    cudaStream_t push[kMaxWorld] = {};
-    cudaEvent_t push_done[kMaxWorld] = {};
-    uint32_t* counters = nullptr;          // kMaxChunks completion counts
     // Barrier words: this rank's [2][kMaxWorld], IPC-exported.  [0][p] receives peer p's
-    // "ready" epoch (p's output may be written: its readers are done), [1][p] its "landed"
-    // epoch (p's pushes into this rank's output are complete).  peer_flags[p] is peer p's
-    // array as mapped here.  The epoch counts overlapped calls; every rank makes the same.
+    // "ready" epoch (p's output may be written: its readers are done); [1][p] counts the
+    // CTAs of p's kernels that have finished storing into this rank's output.  peer_flags[p]
+    // is peer p's array as mapped here.  epoch counts overlapped calls and landed_target the
+    // CTAs each sender has run in them; every rank makes the same calls, so both agree.
     uint32_t* flags = nullptr;
     uint32_t* peer_flags[kMaxWorld] = {};
     uint32_t epoch = 0;
+    uint32_t landed_target = 0;
     // The symmetric output: this rank's [m, n] bf16 buffer, into whose column blocks the
     // kernel and the peers write, and the peers' buffers as mapped here.
     void* xbuf = nullptr;
@@ -77,18 +69,6 @@ struct Comm {
     void* peer_xbuf[kMaxWorld] = {};
     cudaIpcMemHandle_t* handles_dev = nullptr;   // world handles, for the one-off exchange
 };
-
-void destroy_push_streams(Comm* c) {
-    for (int p = 0; p < kMaxWorld; ++p) {
-        if (c->push[p]) {
-            cudaStreamSynchronize(c->push[p]);
-            cudaStreamDestroy(c->push[p]);
-        }
-        if (c->push_done[p]) cudaEventDestroy(c->push_done[p]);
-        c->push[p] = nullptr;
-        c->push_done[p] = nullptr;
-    }
-}
 
 using ValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 
@@ -118,19 +98,19 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
-// One thread per peer waits until the peer's landed word has reached `epoch` (a cyclic
+// One thread per peer waits until the peer's landed count has reached `target` (a cyclic
 // comparison, as CU_STREAM_WAIT_VALUE_GEQ makes), reading it with acquire semantics at
-// system scope: the peer wrote it after its copies into this rank's output, with the
-// memory fence a stream write carries, so the work after this kernel sees those copies.
+// system scope: each of the peer's CTAs added to it with release semantics after its
+// stores into this rank's output, so the work after this kernel sees those stores.
 // Gives up after 2 s (bit 1 of the status word; the output is then incomplete).
-__global__ void wait_landed(const uint32_t* __restrict__ landed, int world, int rank, uint32_t epoch) {
+__global__ void wait_landed(const uint32_t* __restrict__ landed, int world, int rank, uint32_t target) {
     const int p = threadIdx.x;
     if (p >= world || p == rank) return;
     const unsigned long long t0 = globaltimer_ns();
     for (;;) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(landed + p) : "memory");
-        if (static_cast<int32_t>(v - epoch) >= 0) return;
+        if (static_cast<int32_t>(v - target) >= 0) return;
         if (globaltimer_ns() - t0 > 2000000000ull) {
             atomicOr(&g_shard_status, 1u);
             return;
@@ -268,7 +248,10 @@ static int ensure_exchange_buffer(Comm* c, size_t bytes, const char* fn) {
         c->xbuf_cap = bytes;
         return SDQ_OK;
     }
-    cudaError_t e = cudaStreamSynchronize(c->side);
+    // Kernels of earlier calls may still store into the peers' buffers through the mappings
+    // about to be closed, and the peers' into this one: wait for this device's work (a
+    // peer's stores into this buffer have landed once this rank's wait for them is done).
+    cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return fail_cuda("synchronise", e);
     for (int p = 0; p < c->world; ++p)
         if (c->peer_xbuf[p]) {
@@ -316,7 +299,7 @@ __global__ void copy_v1(const uint16_t* __restrict__ src, uint16_t* __restrict__
 }
 
 // The overlapped form of sdq_quantized_matmul_sharded (see the file comment).  Returns
-// kNotOverlapped, having enqueued nothing, when the shape does not split into chunks.
+// kNotOverlapped, having enqueued nothing, when the shape or the world does not suit it.
 static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t m, int64_t k,
                               const uint32_t* wq, const void* scales, const void* biases,
                               sdq_dtype sb_dtype, int64_t n_local, int group_size, int bits,
@@ -326,21 +309,11 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
     int rc = sdq::validate_qmm(x, x_dtype, m, k, wq, scales, biases, sb_dtype, n_local, 1, group_size,
                                bits, "affine", bias_local, y, y_dtype, fn);
     if (rc != SDQ_OK) return rc;
-    if ((n_local * 2) % 16 != 0) return kNotOverlapped;   // 2-D pushes want 16-byte rows
+    // The epilogue stores 16-byte pieces of rows into the peers' copies; one kernel reaches
+    // at most kTcMaxPeers peers.
+    if (n_local % 8 != 0 || c->world - 1 > sdq::kTcMaxPeers) return kNotOverlapped;
     const ValueFn wait = wait_value_fn(), write = write_value_fn();
     if (wait == nullptr || write == nullptr || c->flags == nullptr) return kNotOverlapped;
-    // The compute kernel takes every SM: the barriers below need none.
-    const int grid_cap = sdq::num_sms();
-    const int64_t bt = sdq::qmm_tc_tile_tokens(m, k, n_local, bits, grid_cap);
-    const int64_t ntt = (m + bt - 1) / bt;
-    if (ntt < 2) return kNotOverlapped;
-    // Fewer, larger chunks when there are many peers: every chunk costs a wait and a copy
-    // per peer to enqueue.
-    const int64_t want_chunks = c->world <= 2 ? kChunks : kChunks / 2;
-    int64_t nch = ntt < want_chunks ? ntt : want_chunks;
-    const int64_t tpc = (ntt + nch - 1) / nch;           // token tiles per chunk
-    nch = (ntt + tpc - 1) / tpc;
-    const int64_t nft = (n_local + 127) / 128;
     const size_t total = static_cast<size_t>(m) * ldy;   // elements of [m, n]
     if ((rc = ensure_exchange_buffer(c, total * sizeof(uint16_t), fn)) != SDQ_OK) return rc;
     uint16_t* out = static_cast<uint16_t*>(c->xbuf);     // this rank's copy of [m, n]
@@ -350,37 +323,37 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         return sdq::set_error_message(SDQ_ERR_CUDA, t_shard_msg.c_str());
     };
     const uint32_t epoch = ++c->epoch;
-    // The side stream first waits for everything already on the caller's stream (a reader
-    // of the previous result in the symmetric output among it), then tells every peer that
-    // this rank's output may be written.
-    cudaError_t e = cudaEventRecord(c->ev_entry, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->ev_entry, 0);
-    if (e != cudaSuccess) return cuda_err("stream set-up", e);
+    // Ready: the stream write runs once everything before it on the caller's stream is done
+    // (the readers of the previous result among it), and tells every peer that its stores
+    // into this rank's output may begin.  The kernel then waits for every peer's word.
     for (int p = 0; p < c->world; ++p) {
         if (p == c->rank) continue;
-        if (write(reinterpret_cast<CUstream>(c->side), reinterpret_cast<CUdeviceptr>(c->peer_flags[p] + c->rank),
+        if (write(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(c->peer_flags[p] + c->rank),
                   epoch, 0) != CUDA_SUCCESS)
             return cuda_err("ready flag", cudaErrorUnknown);
     }
-    // The kernel needs no barrier: the previous call's copy out of this rank's output was
-    // joined into the caller's stream.  Each push stream follows the counters' reset and
-    // its peer's ready word.
-    e = cudaMemsetAsync(c->counters, 0, nch * sizeof(uint32_t), st);
-    if (e == cudaSuccess) e = cudaEventRecord(c->ev_start, st);
-    for (int p = 0; e == cudaSuccess && p < c->world; ++p) {
+    for (int p = 0; p < c->world; ++p) {
         if (p == c->rank) continue;
-        e = cudaStreamWaitEvent(c->push[p], c->ev_start, 0);
-        if (e == cudaSuccess &&
-            wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->flags + p), epoch,
+        if (wait(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(c->flags + p), epoch,
                  0 /* GEQ */) != CUDA_SUCCESS)
-            e = cudaErrorUnknown;
+            return cuda_err("ready wait", cudaErrorUnknown);
     }
-    if (e != cudaSuccess) return cuda_err("stream set-up", e);
-    // The kernel writes this rank's block straight into its column block of the output.
+    // The kernel writes this rank's block in place and stores every tile of it into the
+    // same place of each peer's output as it finishes.
+    uint16_t* peers[sdq::kTcMaxPeers];
+    uint32_t* landed[sdq::kTcMaxPeers];
+    int np = 0;
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        peers[np] = static_cast<uint16_t*>(c->peer_xbuf[p]) + static_cast<size_t>(c->rank) * n_local;
+        landed[np] = c->peer_flags[p] + kMaxWorld + c->rank;
+        ++np;
+    }
     const char* msg = nullptr;
-    e = sdq::launch_qmm_tc_signal(x, m, k, wq, scales, biases, n_local, bits, sdq::bias_only(bias_local),
-                                  out + static_cast<size_t>(c->rank) * n_local, ldy, st, &msg,
-                                  c->counters, (int)tpc, (int)nch, grid_cap);
+    int grid = 0;
+    cudaError_t e = sdq::launch_qmm_tc_push(x, m, k, wq, scales, biases, n_local, bits, sdq::bias_only(bias_local),
+                                            out + static_cast<size_t>(c->rank) * n_local, ldy, st, &msg, peers,
+                                            landed, np, 0, &grid);
     if (e != cudaSuccess) {
         if (msg) {
             t_shard_msg = std::string(fn) + ": " + msg;
@@ -388,62 +361,23 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
         }
         return cuda_err("tensor-core kernel", e);
     }
-    // Each finished chunk of rows goes, as one 2-D copy, into the same rows and column
-    // block of every peer's output.
-    const size_t pitch = static_cast<size_t>(ldy) * sizeof(uint16_t);
-    for (int64_t i = 0; i < nch; ++i) {
-        const int64_t t0 = i * tpc, t1 = (i + 1) * tpc < ntt ? (i + 1) * tpc : ntt;
-        const int64_t m0 = t0 * bt, m1 = t1 * bt < m ? t1 * bt : m;
-        const cuuint32_t target = static_cast<cuuint32_t>((t1 - t0) * nft);
-        const size_t off = static_cast<size_t>(m0) * ldy + static_cast<size_t>(c->rank) * n_local;
-        for (int p = 0; p < c->world; ++p) {
-            if (p == c->rank) continue;
-            if (wait(reinterpret_cast<CUstream>(c->push[p]), reinterpret_cast<CUdeviceptr>(c->counters + i),
-                     target, 0 /* GEQ */) != CUDA_SUCCESS)
-                return cuda_err("stream wait on a chunk count", cudaErrorUnknown);
-            uint16_t* dst = static_cast<uint16_t*>(c->peer_xbuf[p]) + off;
-            if ((e = cudaMemcpy2DAsync(dst, pitch, out + off, pitch, n_local * sizeof(uint16_t),
-                                       static_cast<size_t>(m1 - m0), cudaMemcpyDeviceToDevice,
-                                       c->push[p])) != cudaSuccess)
-                return cuda_err("push to a peer", e);
-        }
-    }
-    // After its last copy each push stream writes its peer's landed word (the stream write's
-    // memory fence orders it after the copies); the side stream joins the push streams, so
-    // that the next call's kernel does not overwrite this rank's block before it is read.
-    for (int p = 0; p < c->world; ++p) {
-        if (p == c->rank) continue;
-        if (write(reinterpret_cast<CUstream>(c->push[p]),
-                  reinterpret_cast<CUdeviceptr>(c->peer_flags[p] + kMaxWorld + c->rank), epoch, 0) != CUDA_SUCCESS)
-            return cuda_err("landed flag", cudaErrorUnknown);
-        if ((e = cudaEventRecord(c->push_done[p], c->push[p])) != cudaSuccess ||
-            (e = cudaStreamWaitEvent(c->side, c->push_done[p], 0)) != cudaSuccess)
-            return cuda_err("push join", e);
-    }
-    // This rank's own block is complete once the kernel is (its last chunk's count).
-    if ((e = cudaEventRecord(c->ev_kernel, st)) != cudaSuccess ||
-        (e = cudaStreamWaitEvent(c->side, c->ev_kernel, 0)) != cudaSuccess)
-        return cuda_err("stream join", e);
-    // Every peer's pushes into this rank's output have landed once its landed word holds
-    // the epoch.
-    wait_landed<<<1, kMaxWorld, 0, c->side>>>(c->flags + kMaxWorld, c->world, c->rank, epoch);
+    // Every peer runs as many CTAs as this rank (the same shapes on the same parts); the
+    // output is whole once every peer's count has grown by that many.
+    c->landed_target += static_cast<uint32_t>(grid);
+    wait_landed<<<1, kMaxWorld, 0, st>>>(c->flags + kMaxWorld, c->world, c->rank, c->landed_target);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_err("landed wait", e);
     if (y != out) {
         const int threads = 256;
         const bool v8 = (reinterpret_cast<uintptr_t>(y) % 16) == 0 && total % 8 == 0;
         const int64_t work = v8 ? static_cast<int64_t>(total / 8) : static_cast<int64_t>(total);
-        int64_t grid = (work + threads - 1) / threads;
-        if (grid > 4096) grid = 4096;
+        int64_t g = (work + threads - 1) / threads;
+        if (g > 4096) g = 4096;
         if (v8)
-            copy_v8<<<(int)grid, threads, 0, c->side>>>(reinterpret_cast<const uint4*>(out),
-                                                         static_cast<uint4*>(y), work);
+            copy_v8<<<(int)g, threads, 0, st>>>(reinterpret_cast<const uint4*>(out), static_cast<uint4*>(y), work);
         else
-            copy_v1<<<(int)grid, threads, 0, c->side>>>(out, static_cast<uint16_t*>(y), work);
+            copy_v1<<<(int)g, threads, 0, st>>>(out, static_cast<uint16_t*>(y), work);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_err("output copy", e);
     }
-    e = cudaEventRecord(c->ev_end, c->side);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->ev_end, 0);
-    if (e != cudaSuccess) return cuda_err("stream join", e);
     return sdq::set_error_message(SDQ_OK, "");
 }
 
@@ -478,36 +412,15 @@ int sdq_comm_init(const uint8_t id[128], int world, int rank, void** comm_out) {
         // Resources of the overlapped exchange; if any is missing the plain path runs.
         bool okr = world <= kMaxWorld &&
                    cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->ev_end, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->ev_entry, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->ev_kernel, cudaEventDisableTiming) == cudaSuccess &&
-                   cudaMalloc(reinterpret_cast<void**>(&c->counters), kMaxChunks * sizeof(uint32_t)) ==
-                       cudaSuccess &&
-                   world <= kMaxWorld &&
                    cudaMalloc(reinterpret_cast<void**>(&c->handles_dev), world * sizeof(cudaIpcMemHandle_t)) ==
                        cudaSuccess;
-        for (int p = 0; okr && p < world; ++p)
-            okr = p == rank ||
-                  (cudaStreamCreateWithFlags(&c->push[p], cudaStreamNonBlocking) == cudaSuccess &&
-                   cudaEventCreateWithFlags(&c->push_done[p], cudaEventDisableTiming) == cudaSuccess);
         okr = okr && wait_value_fn() != nullptr && write_value_fn() != nullptr && setup_flags(c);
         if (!okr) {
             cudaGetLastError();
             release_flags(c);
-            destroy_push_streams(c);
-            for (cudaEvent_t* ev : {&c->ev_entry, &c->ev_kernel}) {
-                if (*ev) cudaEventDestroy(*ev);
-                *ev = nullptr;
-            }
             if (c->handles_dev) cudaFree(c->handles_dev);
-            if (c->counters) cudaFree(c->counters);
-            if (c->ev_end) cudaEventDestroy(c->ev_end);
-            if (c->ev_start) cudaEventDestroy(c->ev_start);
             if (c->side) cudaStreamDestroy(c->side);
-            c->counters = nullptr;
             c->handles_dev = nullptr;
-            c->ev_start = c->ev_end = nullptr;
             c->side = nullptr;
         }
     }
@@ -530,18 +443,13 @@ int sdq_comm_destroy(void* comm) {
     if (!comm) return sdq::set_error_message(SDQ_OK, "");
     Comm* c = static_cast<Comm*>(comm);
     if (c->side) {
-        cudaStreamSynchronize(c->side);
+        // This rank's kernels may still store into the peers' outputs through the mappings.
+        cudaDeviceSynchronize();
         for (int p = 0; p < c->world; ++p)
             if (c->peer_xbuf[p]) cudaIpcCloseMemHandle(c->peer_xbuf[p]);
         if (c->xbuf) cudaFree(c->xbuf);
         release_flags(c);
         cudaFree(c->handles_dev);
-        cudaFree(c->counters);
-        destroy_push_streams(c);
-        cudaEventDestroy(c->ev_entry);
-        cudaEventDestroy(c->ev_kernel);
-        cudaEventDestroy(c->ev_end);
-        cudaEventDestroy(c->ev_start);
         cudaStreamDestroy(c->side);
     } else if (c->xbuf) {
         cudaDeviceSynchronize();

@@ -62,7 +62,7 @@ def _free_port() -> int:
         return sk.getsockname()[1]
 
 
-def _rank_main(rank, world, port, m, k, n, bits, q, into_comm_output=False):
+def _rank_main(rank, world, port, m, k, n, bits, q, into_comm_output=False, ms=None):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -75,20 +75,21 @@ def _rank_main(rank, world, port, m, k, n, bits, q, into_comm_output=False):
         comm = sdq.Comm(uid[0], world, rank)
         try:
             wq, s, b = _weights(n, k, bits, "cuda")             # the full weight, on every rank
-            x = _x(m, k, "cuda")
-            full = sdq.quantized_matmul(x, wq, s, b, 64, bits)
             lo, hi = sdq.shard_rows(n, world, rank)
-            args = (x, wq[lo:hi].contiguous(), s[lo:hi].contiguous(), b[lo:hi].contiguous(), comm, 64, bits)
-            target = comm.output(m, n) if into_comm_output else None
             same, rel = True, 0.0
-            for call in range(2):       # the second call reuses the exchange state
-                out, _ = sdq.quantized_matmul_sharded(*args, out=target)
-                torch.cuda.synchronize()
-                sdq.device_status()
-                same = same and torch.equal(out.view(torch.int16), full.view(torch.int16))
-                rel = max(rel, float((out.float() - full.float()).abs().max() / full.float().abs().max()))
-                if target is not None:
-                    assert out.data_ptr() == target.data_ptr()
+            for mi in (ms or [m]):      # several sizes: the exchange buffer grows between them
+                x = _x(mi, k, "cuda")
+                full = sdq.quantized_matmul(x, wq, s, b, 64, bits)
+                args = (x, wq[lo:hi].contiguous(), s[lo:hi].contiguous(), b[lo:hi].contiguous(), comm, 64, bits)
+                target = comm.output(mi, n) if into_comm_output else None
+                for call in range(2):       # the second call reuses the exchange state
+                    out, _ = sdq.quantized_matmul_sharded(*args, out=target)
+                    torch.cuda.synchronize()
+                    sdq.device_status()
+                    same = same and torch.equal(out.view(torch.int16), full.view(torch.int16))
+                    rel = max(rel, float((out.float() - full.float()).abs().max() / full.float().abs().max()))
+                    if target is not None:
+                        assert out.data_ptr() == target.data_ptr()
             q.put((rank, same, rel))
         finally:
             comm.destroy()
@@ -125,6 +126,42 @@ def test_two_gpu_sharded_linear_reassembles_the_full_product(bits, m, into_comm_
         else:
             # M <= 8 runs the weight-stream kernel, whose k-split follows N: tolerance only
             assert rel <= 1e-2, f"rank {rank}: max-abs-rel {rel:.3e}"
+
+
+def _run_ranks(world, *args, **kw):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, *args, q), kwargs=kw) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return sorted(results)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_sharded_linear_with_several_peers(world, bits):
+    """Four and eight ranks: each kernel stores its tiles into three / seven peers' outputs
+    and every rank's assembled output equals the unsharded product bit for bit, over
+    several sizes (the exchange buffer grows between them, and shrinks back into use)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    k, n = 512, 256 * world
+    for rank, same, rel in _run_ranks(world, 300, k, n, bits, ms=[300, 1000, 17, 300]):
+        assert same is not None, f"rank {rank}: {rel}"
+        assert same, f"rank {rank}: sharded product differs (max-abs-rel {rel:.3e})"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_exchange_buffer_grows_between_sizes():
+    for rank, same, rel in _run_ranks(2, 64, 512, 1024, 4, into_comm_output=True, ms=[64, 2048, 100]):
+        assert same is not None, f"rank {rank}: {rel}"
+        assert same, f"rank {rank}: sharded product differs (max-abs-rel {rel:.3e})"
 
 
 def _static_rank_main(rank, world, port, m, k, n, bits, q):
