@@ -78,16 +78,20 @@ struct TcCfg;
 // The exchange of a column-sharded output, fused into the epilogue (npeers > 0): besides
 // this rank's copy, each finished output tile is stored at the same place of every peer's
 // copy of the [M, world * N] output (peer[i] points at this rank's column block there,
-// rows ldy elements apart, over NVLink).  When a CTA has finished its tiles it adds 1 to
-// landed[i], a word in peer i's memory, after a system-scope fence, so a peer that has
-// counted every CTA of every sender sees the whole output.  A CTA that gave up counts
-// too (the status word carries the error), so no peer waits for it.  grid_out (host side
-// only) receives the number of CTAs launched.
+// rows ldy elements apart), by TMA tensor stores over NVLink through one tensor map per
+// peer (PeerMaps).  When a CTA has finished its tiles and its stores have completed, it
+// adds 1 to landed[i], a word in peer i's memory, after a system-scope fence, so a peer
+// that has counted every CTA of every sender sees the whole output.  A CTA that gave up
+// counts too (the status word carries the error), so no peer waits for it.  grid_out
+// (host side only) receives the number of CTAs launched.
 struct TcSignal {
     int npeers = 0;
     uint16_t* peer[kTcMaxPeers] = {};
     uint32_t* landed[kTcMaxPeers] = {};
     int* grid_out = nullptr;
+};
+struct PeerMaps {
+    CUtensorMap map[kTcMaxPeers];
 };
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
                   const uint16_t* __restrict__ biases, const EpiArgs epi,
                   uint16_t* y, int M, int N, int K, int64_t ldy, int y_tma, int r_tma,
-                  const TcSignal sig) {
+                  const TcSignal sig, const __grid_constant__ PeerMaps pm) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -474,9 +478,15 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
             if (y_tma) {
                 if (leader) {
                     for (int c = e; c < NCH; c += kEpiGroups)
-                        if (tt * BT + c * CW < M)
+                        if (tt * BT + c * CW < M) {
                             tma_store_2d(&tmY, sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
                                          tt * BT + c * CW);
+#pragma unroll
+                            for (int i = 0; i < kTcMaxPeers; ++i)
+                                if (i < sig.npeers)
+                                    tma_store_2d(&pm.map[i], sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
+                                                 tt * BT + c * CW);
+                        }
                     bulk_commit_group();
                 }
             } else if (!YF32 && f < N) {
@@ -488,43 +498,18 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                     for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * ldy + f] = yrow[r * C::BF];
                 }
             }
-            if constexpr (!YF32) {
-                if (sig.npeers > 0) {
-                    // The staged tile, 16 bytes per thread and store, into every peer's copy
-                    // (rows past M and pieces past N are not stored; N % 8 == 0).
-                    constexpr int PR = C::BF / 8;                 // 16-byte pieces per row
-                    for (int c = e; c < NCH; c += kEpiGroups) {
-                        const int t0 = tt * BT + c * CW;
-                        const uint8_t* src = sY + (size_t)c * CW * C::BF * 2;
-                        for (int pc = fl; pc < CW * PR; pc += 128) {
-                            const int r = pc / PR, q = pc - r * PR;
-                            const int t = t0 + r, f8 = ft * C::BF + 8 * q;
-                            if (t < M && f8 < N) {
-                                const uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)r * C::BF * 2 + 16 * q);
-                                const size_t off = (size_t)t * ldy + f8;
-#pragma unroll
-                                for (int i = 0; i < kTcMaxPeers; ++i)
-                                    if (i < sig.npeers) *reinterpret_cast<uint4*>(sig.peer[i] + off) = v;
-                            }
-                        }
-                    }
-                }
-            }
         }
         if (leader && y_tma) bulk_wait_group0();
-        if (sig.npeers > 0) {
-            // Every store of this CTA into the peers' copies is visible before their landed
-            // words count the CTA: each thread's fence orders its stores before the group
-            // barrier, and the leader releases at system scope after it.
+        if (sig.npeers > 0 && leader) {
+            // The leader issued every store of this CTA into the peers' copies and has seen
+            // them complete; it releases at system scope after a proxy and a system fence,
+            // so a peer that acquires its landed word sees them.
+            asm volatile("fence.proxy.async.global;" ::: "memory");
             __threadfence_system();
-            named_barrier_sync(1 + e, 128);
-            if (leader) {
-                __threadfence_system();
 #pragma unroll
-                for (int i = 0; i < kTcMaxPeers; ++i)
-                    if (i < sig.npeers)
-                        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(sig.landed[i]) : "memory");
-            }
+            for (int i = 0; i < kTcMaxPeers; ++i)
+                if (i < sig.npeers)
+                    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(sig.landed[i]) : "memory");
         }
     }
 
@@ -599,6 +584,28 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
             return cudaErrorInvalidValue;
         }
     }
+    // One tensor map per peer copy of the output, the same shape and pitch as Y's.
+    PeerMaps pm;
+    std::memset(&pm, 0, sizeof(pm));
+    if (sig.npeers > 0) {
+        if (!y_tma || FUSED || YF32) {
+            *msg = "the fused exchange needs a bf16, TMA-stored plain output";
+            return cudaErrorInvalidValue;
+        }
+        for (int i = 0; i < sig.npeers; ++i) {
+            cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+            cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
+            cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)C::CW};
+            cuuint32_t estr[2] = {1, 1};
+            CUresult r = enc(&pm.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sig.peer[i], dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) {
+                *msg = "cuTensorMapEncodeTiled rejected a peer's output tensor map";
+                return cudaErrorInvalidValue;
+            }
+        }
+    }
     // The residual ([m, n], contiguous) is copied in by TMA under the same conditions.
     CUtensorMap tmR;
     std::memset(&tmR, 0, sizeof(tmR));
@@ -636,7 +643,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
-        ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig);
+        ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig, pm);
     return cudaGetLastError();
 }
 
