@@ -90,9 +90,12 @@ def quantize(w: torch.Tensor, group_size: int = GROUP_SIZE, bits: int = 4, strea
 
 
 def dequantize(wq, scales, biases, group_size: int = GROUP_SIZE, bits: int = 4,
-               out_dtype=torch.bfloat16, stream=None) -> torch.Tensor:
-    """``mlx_dequantize`` replacement: reconstruct [n, k] (one rounding of s*q + b)."""
+               out_dtype=None, stream=None) -> torch.Tensor:
+    """``mlx_dequantize`` replacement: reconstruct [n, k] (one rounding of s*q + b).  The
+    output dtype defaults to the scales' dtype, as MLX's does (mlx.rs:1935-1938)."""
     _need_cuda(wq, scales, biases)
+    if out_dtype is None:
+        out_dtype = scales.dtype
     n = wq.shape[0]
     k = wq.shape[1] * 32 // bits
     out = torch.empty((n, k), device=wq.device, dtype=out_dtype)
@@ -273,7 +276,7 @@ class QuantizedArray:
         wq, s, b = quantize(w, group_size, bits, stream, sb_dtype)
         return cls(wq, s, b, group_size, bits)
 
-    def dequantize(self, out_dtype=torch.bfloat16, stream=None) -> torch.Tensor:
+    def dequantize(self, out_dtype=None, stream=None) -> torch.Tensor:
         """Reconstruct the dense array -- for tests, not the hot path (mlx.rs:1913-1918)."""
         return dequantize(self.weight, self.scales, self.biases, self.group_size, self.bits,
                           out_dtype, stream)

@@ -89,7 +89,9 @@ def test_f32_scales_that_are_not_bf16_values_are_rounded():
     b32 = (b16.float().cpu() * (1 + 1e-3 * torch.rand(b16.shape, generator=g))).cuda()
     sr = torch.from_numpy(rne_bf16(s32).view(np.int16)).cuda().view(torch.bfloat16)
     br = torch.from_numpy(rne_bf16(b32).view(np.int16)).cuda().view(torch.bfloat16)
-    assert torch.equal(sdq.dequantize(wq, s32, b32, 64, bits), sdq.dequantize(wq, sr, br, 64, bits))
+    assert torch.equal(sdq.dequantize(wq, s32, b32, 64, bits, out_dtype=torch.bfloat16),
+                       sdq.dequantize(wq, sr, br, 64, bits))
+    assert sdq.dequantize(wq, s32, b32, 64, bits).dtype == torch.float32    # the scales' dtype
     x = torch.randn(20, k, generator=g).cuda().to(torch.bfloat16)
     assert torch.equal(sdq.quantized_matmul(x, wq, s32, b32, 64, bits),
                        sdq.quantized_matmul(x, wq, sr, br, 64, bits))
