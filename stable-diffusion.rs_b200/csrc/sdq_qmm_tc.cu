@@ -77,21 +77,40 @@ struct TcCfg;
 
 // The exchange of a column-sharded output, fused into the epilogue (npeers > 0): besides
 // this rank's copy, each finished output tile is stored at the same place of every peer's
-// copy of the [M, world * N] output (peer[i] points at this rank's column block there,
+// copy of the [M, world * N] output (peers[i] points at this rank's column block there,
 // rows ldy elements apart), by TMA tensor stores over NVLink through one tensor map per
-// peer (PeerMaps).  When a CTA has finished its tiles and its stores have completed, it
-// adds 1 to landed[i], a word in peer i's memory, after a system-scope fence, so a peer
-// that has counted every CTA of every sender sees the whole output.  A CTA that gave up
-// counts too (the status word carries the error), so no peer waits for it.  grid_out
-// (host side only) receives the number of CTAs launched.
+// peer.  When a CTA has finished its tiles and its stores have completed, it adds 1 to
+// landed[i], a word in peer i's memory, after a system-scope fence, so a peer that has
+// counted every CTA of every sender sees the whole output.  A CTA that gave up counts
+// too (the status word carries the error), so no peer waits for it.  grid_out receives
+// the number of CTAs launched.  (Host side; the kernel gets PeerArg.)
 struct TcSignal {
     int npeers = 0;
-    uint16_t* peer[kTcMaxPeers] = {};
-    uint32_t* landed[kTcMaxPeers] = {};
+    uint16_t* const* peers = nullptr;
+    uint32_t* const* landed = nullptr;
     int* grid_out = nullptr;
 };
-struct PeerMaps {
+// The kernel's view of it.  Only the pushing instantiation carries the tensor maps: the
+// others' parameters stay small (a launch's parameter block is copied for every launch,
+// and 900 more bytes of it cost about a microsecond per launch of the short kernels).
+template <bool PUSH>
+struct PeerArg {
     CUtensorMap map[kTcMaxPeers];
+    uint32_t* landed[kTcMaxPeers];
+    int npeers;
+};
+// The other instantiations carry an optional per-chunk completion count instead: token tile
+// tt belongs to chunk tt / chunk_tts, and once a tile's Y is in global memory the epilogue
+// adds 1 to done[chunk] (done == nullptr, as every current call passes, turns it off).  It
+// stays because of what it does to the compiled kernel: with it, ptxas gives config 2's
+// kernel 106 registers and the launch takes 256-258 us on a B200; without it, 104
+// registers and 262-264 us (the two builds timed alternately on one box).
+template <>
+struct PeerArg<false> {
+    int npeers;
+    uint32_t* done;
+    int chunk_tts;
+    int nchunks;
 };
 
 template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
@@ -125,14 +144,16 @@ size_t smem_bytes(int64_t k) {
 // FUSED: the output stage applies gate / residual / activation (EpiArgs::fused); the plain
 // instantiation adds the bias only and carries none of that code.  YF32 (plain only): the
 // output is f32, written from the accumulator straight to global memory (bias in f32).
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32>
+// PUSH (plain bf16 only): the epilogue also stores every tile into the peers' outputs
+// (TcSignal); the other instantiations carry none of that code.
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32, bool PUSH>
 __global__ void __launch_bounds__(tc_threads(BITS), 1)
     qmm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                   const uint16_t* __restrict__ xg, const uint16_t* __restrict__ scales,
                   const uint16_t* __restrict__ biases, const EpiArgs epi,
                   uint16_t* y, int M, int N, int K, int64_t ldy, int y_tma, int r_tma,
-                  const TcSignal sig, const __grid_constant__ PeerMaps pm) {
+                  const __grid_constant__ PeerArg<PUSH> pa) {
     using C = TcCfg<BITS, BT, SX, SW, SA, XRES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -481,11 +502,13 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                         if (tt * BT + c * CW < M) {
                             tma_store_2d(&tmY, sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
                                          tt * BT + c * CW);
+                            if constexpr (PUSH) {
 #pragma unroll
-                            for (int i = 0; i < kTcMaxPeers; ++i)
-                                if (i < sig.npeers)
-                                    tma_store_2d(&pm.map[i], sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
-                                                 tt * BT + c * CW);
+                                for (int i = 0; i < kTcMaxPeers; ++i)
+                                    if (i < pa.npeers)
+                                        tma_store_2d(&pa.map[i], sY + (size_t)c * CW * C::BF * 2, ft * C::BF,
+                                                     tt * BT + c * CW);
+                            }
                         }
                     bulk_commit_group();
                 }
@@ -498,18 +521,36 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
                     for (int r = 0; r < nr; ++r) y[(size_t)(t0 + r) * ldy + f] = yrow[r * C::BF];
                 }
             }
+            if constexpr (!PUSH) {
+                if (pa.done != nullptr) {
+                    // This tile's Y must be in global memory before its chunk counts it.
+                    if (y_tma) {
+                        if (leader) {
+                            bulk_wait_group0();
+                            __threadfence();
+                            atomicAdd(pa.done + tt / pa.chunk_tts, 1u);
+                        }
+                    } else {
+                        __threadfence();
+                        named_barrier_sync(1 + e, 128);
+                        if (leader) atomicAdd(pa.done + tt / pa.chunk_tts, 1u);
+                    }
+                }
+            }
         }
         if (leader && y_tma) bulk_wait_group0();
-        if (sig.npeers > 0 && leader) {
-            // The leader issued every store of this CTA into the peers' copies and has seen
-            // them complete; it releases at system scope after a proxy and a system fence,
-            // so a peer that acquires its landed word sees them.
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            __threadfence_system();
+        if constexpr (PUSH) {
+            if (leader) {
+                // The leader issued every store of this CTA into the peers' copies and has
+                // seen them complete; it releases at system scope after a proxy and a system
+                // fence, so a peer that acquires its landed word sees them.
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                __threadfence_system();
 #pragma unroll
-            for (int i = 0; i < kTcMaxPeers; ++i)
-                if (i < sig.npeers)
-                    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(sig.landed[i]) : "memory");
+                for (int i = 0; i < kTcMaxPeers; ++i)
+                    if (i < pa.npeers)
+                        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pa.landed[i]) : "memory");
+            }
         }
     }
 
@@ -520,6 +561,13 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
+    if constexpr (!PUSH) {
+        // A CTA that gave up raises every chunk to its maximum, so that nothing waiting on a
+        // count is left waiting (the status word carries the error).
+        if (threadIdx.x == 0 && pa.done != nullptr && *abort_flag) {
+            for (int i = 0; i < pa.nchunks; ++i) atomicMax(pa.done + i, 0x7FFFFFFFu);
+        }
+    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -527,7 +575,7 @@ __global__ void __launch_bounds__(tc_threads(BITS), 1)
 constexpr size_t kMaxSmem = kQmvMaxSmem;
 
 
-template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32>
+template <int BITS, int BT, int SX, int SW, int SA, bool XRES, bool FUSED, bool YF32, bool PUSH>
 cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
                         cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
@@ -585,19 +633,21 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
         }
     }
     // One tensor map per peer copy of the output, the same shape and pitch as Y's.
-    PeerMaps pm;
-    std::memset(&pm, 0, sizeof(pm));
-    if (sig.npeers > 0) {
-        if (!y_tma || FUSED || YF32) {
-            *msg = "the fused exchange needs a bf16, TMA-stored plain output";
+    PeerArg<PUSH> pa;
+    std::memset(&pa, 0, sizeof(pa));
+    if constexpr (PUSH) {
+        if (!y_tma || sig.npeers < 1 || sig.npeers > kTcMaxPeers) {
+            *msg = "the fused exchange needs a TMA-stored output and 1 to 7 peers";
             return cudaErrorInvalidValue;
         }
+        pa.npeers = sig.npeers;
         for (int i = 0; i < sig.npeers; ++i) {
+            pa.landed[i] = sig.landed[i];
             cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
             cuuint64_t strides[1] = {(cuuint64_t)ldy * 2};
             cuuint32_t box[2] = {(cuuint32_t)C::BF, (cuuint32_t)C::CW};
             cuuint32_t estr[2] = {1, 1};
-            CUresult r = enc(&pm.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sig.peer[i], dims, strides, box,
+            CUresult r = enc(&pa.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, sig.peers[i], dims, strides, box,
                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) {
@@ -631,7 +681,7 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     if (e != cudaSuccess) return e;
     static bool configured[64] = {};
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32>,
+        e = cudaFuncSetAttribute(qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32, PUSH>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -640,10 +690,10 @@ cudaError_t launch_tc_t(const void* x, int64_t m, int64_t k, const uint32_t* wq,
     const int64_t cap = grid_cap > 0 && grid_cap < num_sms() ? grid_cap : num_sms();
     const int grid = (int)(tiles < cap ? tiles : cap);
     if (sig.grid_out) *sig.grid_out = grid;
-    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32><<<grid, tc_threads(BITS), smem, st>>>(
+    qmm_tc_kernel<BITS, BT, SX, SW, SA, XRES, FUSED, YF32, PUSH><<<grid, tc_threads(BITS), smem, st>>>(
         tmX, tmW, tmY, tmR, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(scales),
         static_cast<const uint16_t*>(biases), epi, static_cast<uint16_t*>(y), (int)m, (int)n, (int)k,
-        ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, sig, pm);
+        ldy, y_tma ? 1 : 0, r_tma ? 1 : 0, pa);
     return cudaGetLastError();
 }
 
@@ -682,14 +732,19 @@ template <int BITS, int BT, int SX, int SW, int SA, bool XRES>
 cudaError_t launch_tc_f(const void* x, int64_t m, int64_t k, const uint32_t* wq, const void* scales,
                         const void* biases, int64_t n, const EpiArgs& epi, void* y, int64_t ldy,
                         cudaStream_t st, const char** msg, const TcSignal& sig, int grid_cap) {
+    if (sig.npeers > 0) {  // the sharded linear: plain bf16 output stage, tiles pushed to peers
+        if (epi.fused() || epi.f32) return cudaErrorInvalidValue;
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, false, true>(x, m, k, wq, scales, biases, n, epi, y,
+                                                                           ldy, st, msg, sig, grid_cap);
+    }
     if (epi.fused())
-        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, true, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
-                                                                    msg, sig, grid_cap);
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, true, false, false>(x, m, k, wq, scales, biases, n, epi, y,
+                                                                           ldy, st, msg, sig, grid_cap);
     if (epi.f32)           // f32 output (the bias, if any, f32 too)
-        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, true>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
-                                                                    msg, sig, grid_cap);
-    return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, false>(x, m, k, wq, scales, biases, n, epi, y, ldy, st,
-                                                                 msg, sig, grid_cap);
+        return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, true, false>(x, m, k, wq, scales, biases, n, epi, y,
+                                                                           ldy, st, msg, sig, grid_cap);
+    return launch_tc_t<BITS, BT, SX, SW, SA, XRES, false, false, false>(x, m, k, wq, scales, biases, n, epi, y,
+                                                                        ldy, st, msg, sig, grid_cap);
 }
 
 template <int BITS>
@@ -744,13 +799,11 @@ cudaError_t launch_qmm_tc_push(const void* x, int64_t m, int64_t k, const uint32
                                const EpiArgs& epi, void* y, int64_t ldy, cudaStream_t st,
                                const char** msg, uint16_t* const* peers, uint32_t* const* landed,
                                int npeers, int grid_cap, int* grid_out) {
-    if (npeers < 0 || npeers > kTcMaxPeers) return cudaErrorInvalidValue;
+    if (npeers < 1 || npeers > kTcMaxPeers) return cudaErrorInvalidValue;
     TcSignal sig{};
     sig.npeers = npeers;
-    for (int i = 0; i < npeers; ++i) {
-        sig.peer[i] = peers[i];
-        sig.landed[i] = landed[i];
-    }
+    sig.peers = peers;
+    sig.landed = landed;
     sig.grid_out = grid_out;
     return bits == 4 ? launch_tc_bits<4>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap)
                      : launch_tc_bits<8>(x, m, k, wq, scales, biases, n, epi, y, ldy, st, msg, sig, grid_cap);
