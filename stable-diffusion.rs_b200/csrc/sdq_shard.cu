@@ -339,12 +339,14 @@ static int sharded_overlapped(Comm* c, const void* x, sdq_dtype x_dtype, int64_t
             return cuda_err("ready wait", cudaErrorUnknown);
     }
     // The kernel writes this rank's block in place and stores every tile of it into the
-    // same place of each peer's output as it finishes.
+    // same place of each peer's output as it finishes.  Each rank walks its peers starting
+    // from the next rank up, so that the ranks' first stores of a chunk go to different GPUs
+    // rather than all to the lowest rank.
     uint16_t* peers[sdq::kTcMaxPeers];
     uint32_t* landed[sdq::kTcMaxPeers];
     int np = 0;
-    for (int p = 0; p < c->world; ++p) {
-        if (p == c->rank) continue;
+    for (int j = 1; j < c->world; ++j) {
+        const int p = (c->rank + j) % c->world;
         peers[np] = static_cast<uint16_t*>(c->peer_xbuf[p]) + static_cast<size_t>(c->rank) * n_local;
         landed[np] = c->peer_flags[p] + kMaxWorld + c->rank;
         ++np;
